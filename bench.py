@@ -1,0 +1,329 @@
+"""Decode benchmark: Qwen2-0.5B architecture, Q8_0 weights, batch 1, greedy.
+
+    python bench.py [--gpus N] [--steps K] [--warmup W] [--impl reference]
+
+A step decodes 128 tokens (positions 64..191 after a 64-token prompt) through
+the device session (one CUDA graph per token, token fed back on the device).
+  value  tokens/s with everything resident in HBM (CUDA events on the library
+         stream, max over ranks); weights (528 MB/token) exceed the 126 MB L2,
+         so no flush is needed between steps
+  e2e    the same through mlb_session_generate with host buffers: the step's
+         start token copied host->device and the 128 generated ids copied back
+  roofline  the dominant kernel (the Q8_0 GEMV) timed alone on the lm_head
+         shape [151936, 896]: algorithmic bytes / CUDA-event time vs measured HBM
+  cpu_baseline  the reference CPU implementation (RunBenchmark, built from the
+         reference sources into oracle/_ref) on a bounded sample
+With N > 1 (torchrun) every GPU decodes its own sequence (replicas; weak scaling).
+--impl reference times the reference CPU implementation alone.
+"""
+from __future__ import annotations
+
+import argparse
+import json
+import os
+import statistics
+import subprocess
+import sys
+import time
+
+ROOT = os.path.dirname(os.path.abspath(__file__))
+sys.path.insert(0, ROOT)
+
+METRIC = "decode tok/s (Qwen2-0.5B-arch Q8_0, bs1)"
+UNIT = "tokens/s"
+PROMPT = 64
+NEW = 128
+QWEN2 = dict(vocab_size=151936, dim=896, hidden_dim=4864, n_layers=24, n_heads=14, n_kv_heads=2,
+             head_dim=64, max_seq_len=256, rope_theta=1e6, rms_norm_eps=1e-6, rope_neox=1,
+             qkv_bias=1, tied_embedding=1, qtype=1, seed=3, prompt_seed=3)
+
+
+def algorithmic_bytes_per_token(pos: int) -> int:
+    """Weight bytes + fp32 norms/biases/embedding row + KV read/write at position pos."""
+    D, F, V, L = 896, 4864, 151936, 24
+    qd, kd = 14 * 64, 2 * 64
+    blk = lambda r, c: r * ((c + 31) // 32) * 34  # noqa: E731
+    layer = blk(qd, D) + 2 * blk(kd, D) + blk(D, qd) + 2 * blk(F, D) + blk(D, F)
+    small = L * (2 * D + qd + 2 * kd) * 4 + D * 4 + D * 4  # norms, biases, final norm, embedding row
+    kv = L * (pos + 1) * 2 * kd * 4 + L * 2 * kd * 4       # read 0..pos, write pos
+    return L * layer + blk(V, D) + small + kv
+
+
+CONFIG = {"workload": "Qwen2-0.5B-arch Q8_0 random-init, batch 1, prompt 64 + 128 greedy decode",
+          "model": "qwen2-0.5b-arch", "weights": "Q8_0 (lm_head tied, Q8_0)", "global_batch": 1,
+          "seq_len": PROMPT + NEW, "decode_tokens_per_step": NEW,
+          "l2": "inputs larger than L2 (528 MB of weights streamed per token)"}
+
+
+class Clocks:
+    QUERY = ("index,clocks.sm,clocks.max.sm,power.draw,clocks_event_reasons.active,"
+             "clocks_event_reasons.hw_slowdown,clocks_event_reasons.hw_thermal_slowdown,"
+             "clocks_event_reasons.sw_thermal_slowdown,clocks_event_reasons.sw_power_cap")
+
+    def __init__(self, gpu_index: int):
+        self.gpu = gpu_index
+        self.proc = None
+
+    def start(self):
+        try:
+            self.proc = subprocess.Popen(
+                ["nvidia-smi", f"--id={self.gpu}", f"--query-gpu={self.QUERY}",
+                 "--format=csv,noheader,nounits", "-lms", "200"],
+                stdout=subprocess.PIPE, stderr=subprocess.DEVNULL, text=True)
+        except OSError:
+            self.proc = None
+
+    def stop(self) -> dict:
+        if self.proc is None:
+            return {"sm_mhz": None, "sm_max_mhz": None, "reasons": ["nvidia-smi unavailable"]}
+        time.sleep(0.25)
+        self.proc.terminate()
+        out, _ = self.proc.communicate(timeout=10)
+        sm, mx, reasons = [], None, set()
+        names = ["hw_slowdown", "hw_thermal_slowdown", "sw_thermal_slowdown", "sw_power_cap"]
+        for line in out.splitlines():
+            f = [x.strip() for x in line.split(",")]
+            if len(f) < 9:
+                continue
+            try:
+                sm.append(float(f[1]))
+                mx = float(f[2])
+            except ValueError:
+                continue
+            for name, val in zip(names, f[5:9]):
+                if val.lower() == "active":
+                    reasons.add(name)
+        return {"sm_mhz": statistics.median(sm) if sm else None, "sm_max_mhz": mx,
+                "reasons": sorted(reasons), "samples": len(sm)}
+
+
+def measured_peaks() -> dict:
+    path = os.path.join(ROOT, "MEASURED_PEAKS.json")
+    if os.path.exists(path):
+        with open(path) as f:
+            d = json.load(f)
+        return {"hbm_gbs": d["hbm_gbs"], "source": "measured"}
+    return {"hbm_gbs": 6650.0, "source": "fallback"}
+
+
+def committed_traffic(name: str):
+    path = os.path.join(ROOT, "profiles", "traffic.json")
+    if os.path.exists(path):
+        with open(path) as f:
+            return json.load(f).get(name)
+    return None
+
+
+def reference_sample(threads: int, steps: int, warmup: int, prompt_len=8, n_predict=9):
+    from oracle.binding import run_ref_bench
+    recs = run_ref_bench("qwen2", threads, prompt_len, n_predict, steps, warmup)
+    timed = [r for r in recs if r.get("event") == "step" and r.get("timed")]
+    vals = [r["decode_tok_s"] for r in timed]
+    return statistics.mean(vals) if vals else None, timed
+
+
+def run_reference(args):
+    rank = int(os.environ.get("RANK", "0"))
+    if rank != 0:
+        return 0
+    threads = os.cpu_count() or 1
+    sample = f"reference RunBenchmark on the same model: prompt 8 tokens, 8 decode tokens per step"
+    try:
+        value, timed = reference_sample(threads, args.steps, args.warmup)
+    except Exception as e:  # the harness is built here from the reference tree
+        print(json.dumps({"impl": "reference", "unavailable": f"reference harness failed: {e}"}))
+        return 0
+    ms = statistics.mean(r["decode_ms"] for r in timed) if timed else None
+    line = {"metric": METRIC, "value": value, "unit": UNIT, "n_gpus": args.gpus,
+            "steps": args.steps, "warmup": args.warmup, "ms_per_step": ms,
+            "higher_is_better": True, "scaling": "weak", "vs_baseline": None, "dtype": "f32",
+            "data": "synthetic", "impl": "reference", "config": CONFIG,
+            "cpu_baseline": {"value": value, "unit": UNIT, "cores": threads, "kind": "reference",
+                             "sample": sample},
+            "e2e": {"value": value, "unit": UNIT, "h2d_bytes_per_step": 0,
+                    "d2h_bytes_per_step": 0}}
+    print(json.dumps(line), flush=True)
+    return 0
+
+
+def gemv_roofline(lib, dev, torch, stream):
+    """Times the Q8_0 GEMV alone on the lm_head shape (M = 1) with CUDA events."""
+    import numpy as np
+
+    from mini_llama_b200.device import DeviceArray
+    N, K = 151936, 896
+    nb = K // 32
+    wbytes = N * nb * 34
+    w = lib.malloc(dev, wbytes)
+    scratch = lib.malloc(dev, N * K * 4)
+    lib.call("mlb_synth_normal", dev, scratch, N * K, 2, 8, 0.02)
+    lib.call("mlb_quantize", dev, 1, scratch, N, K, w)
+    x = DeviceArray.from_host(lib, dev, np.ones(K, np.float32))
+    y = DeviceArray(lib, dev, N)
+    flush = lib.malloc(dev, 256 << 20)  # > L2: each launch reads the weights from HBM
+    for _ in range(3):
+        lib.call("mlb_q80_linear", dev, x.ptr, w, N * nb, 1, K, N, None, y.ptr)
+    reps, total = 20, 0.0
+    for _ in range(reps):
+        lib.call("mlb_memset", dev, flush, 1, 256 << 20)
+        e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        e0.record(stream)
+        lib.call("mlb_q80_linear", dev, x.ptr, w, N * nb, 1, K, N, None, y.ptr)
+        e1.record(stream)
+        e1.synchronize()
+        total += e0.elapsed_time(e1) / 1e3
+    lib.sync(dev)
+    for p in (w, scratch, flush):
+        lib.free(dev, p)
+    per_launch = total / reps
+    algo = wbytes + K * 4 + N * 4
+    return algo, per_launch
+
+
+def run_ours(args):
+    import numpy as np
+    import torch
+
+    from mini_llama_b200 import capi
+    from mini_llama_b200.device import DeviceArray, Model, Session
+
+    world = int(os.environ.get("WORLD_SIZE", "1"))
+    rank = int(os.environ.get("RANK", "0"))
+    local = int(os.environ.get("LOCAL_RANK", "0"))
+    torch.cuda.set_device(local)
+    dist = None
+    if world > 1:
+        import datetime
+
+        import torch.distributed as dist
+        dist.init_process_group("nccl", timeout=datetime.timedelta(seconds=300))
+    lib = capi.load()
+    dev = local
+    stream = torch.cuda.ExternalStream(lib.stream(dev), device=torch.device("cuda", dev))
+
+    model = Model(lib, dev, QWEN2)
+    model.synthesize(seed=QWEN2["seed"], tied=True)
+    sess = Session(model)
+    from oracle.binding import Oracle  # only for the prompt ids (seeded generator)
+    prompt = Oracle().tokens(PROMPT, QWEN2["prompt_seed"], QWEN2["vocab_size"])
+    first = sess.generate(prompt, 1)  # prefill, first greedy token at position 64
+    toks = DeviceArray(lib, dev, NEW + 1, np.int32)
+    init = np.zeros(NEW + 1, np.int32)
+    init[0] = first[0]
+    toks.upload(init)
+
+    def step():
+        sess.decode_device(toks.ptr, PROMPT, NEW)
+
+    def barrier():
+        torch.cuda.synchronize(dev)
+        lib.sync(dev)
+        if dist is not None:
+            dist.barrier()
+
+    for _ in range(args.warmup):
+        step()
+    barrier()
+    clocks = Clocks(dev)
+    clocks.start()
+    e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    e0.record(stream)
+    for _ in range(args.steps):
+        step()
+    e1.record(stream)
+    e1.synchronize()
+    barrier()
+    clk = clocks.stop()
+    secs = e0.elapsed_time(e1) / 1e3
+    if dist is not None:
+        t = torch.tensor([secs], device=f"cuda:{dev}")
+        dist.all_reduce(t, op=dist.ReduceOp.MAX)
+        secs = float(t.item())
+    value = world * NEW * args.steps / secs
+
+    # e2e: host start token in, host token ids out, through mlb_session_generate
+    start = torch.empty(1, dtype=torch.int32, pin_memory=True)
+    out = torch.empty(NEW, dtype=torch.int32, pin_memory=True)
+    start[0] = int(first[0])
+
+    def e2e_step():
+        lib.call("mlb_session_generate", sess.handle, start.data_ptr(), 1, PROMPT, NEW,
+                 out.data_ptr())
+
+    for _ in range(max(1, args.warmup)):
+        e2e_step()
+    barrier()
+    t0 = time.perf_counter()
+    for _ in range(args.steps):
+        e2e_step()
+    barrier()
+    e2e_secs = time.perf_counter() - t0
+    if dist is not None:
+        t = torch.tensor([e2e_secs], device=f"cuda:{dev}")
+        dist.all_reduce(t, op=dist.ReduceOp.MAX)
+        e2e_secs = float(t.item())
+    e2e = world * NEW * args.steps / e2e_secs
+
+    peaks = measured_peaks()
+    algo, launch_s = gemv_roofline(lib, dev, torch, stream)
+    achieved = algo / launch_s / 1e9
+    step_bytes = sum(algorithmic_bytes_per_token(p) for p in range(PROMPT, PROMPT + NEW))
+    step_gbs = step_bytes * args.steps / (secs / world * world) / 1e9 if world == 1 else None
+    launches_per_token = 1 + 5 * QWEN2["n_layers"] + 1
+
+    sess.close()
+    model.close()
+    if dist is not None:
+        dist.barrier()
+        dist.destroy_process_group()
+    if rank != 0:
+        return 0
+    cpu = None
+    if world == 1 and not args.no_cpu_baseline:
+        threads = os.cpu_count() or 1
+        try:
+            v, _ = reference_sample(threads, 1, 1)
+            cpu = {"value": v, "unit": UNIT, "cores": threads, "kind": "reference",
+                   "sample": "reference RunBenchmark, prompt 8 + 8 decode tokens, 1 timed step"}
+        except Exception as e:
+            cpu = {"value": None, "unit": UNIT, "cores": threads, "kind": "reference",
+                   "sample": f"unavailable: {e}"}
+    line = {
+        "metric": METRIC, "value": value, "unit": UNIT, "n_gpus": world, "steps": args.steps,
+        "warmup": args.warmup, "ms_per_step": secs / args.steps * 1e3, "higher_is_better": True,
+        "scaling": "weak", "vs_baseline": None, "dtype": "f32 activations, Q8_0 weights",
+        "data": "synthetic (seeded random-init weights and prompt ids)",
+        "config": dict(CONFIG, parallelism=f"replicas x{world}" if world > 1 else "single GPU"),
+        "e2e": {"value": e2e, "unit": UNIT, "h2d_bytes_per_step": 4 + 8 + 4,
+                "d2h_bytes_per_step": NEW * 4 + 4},
+        "roofline": {"bound": "hbm", "kernel": "GemvKernel<Q8_0, M=1> on [151936, 896]",
+                     "achieved": achieved, "peak": peaks["hbm_gbs"], "unit": "GB/s",
+                     "frac": achieved / peaks["hbm_gbs"], "peak_source": peaks["source"],
+                     "bytes_per_launch": algo, "launch_us": launch_s * 1e6,
+                     "traffic": committed_traffic("gemv_q80_lm_head")},
+        "step_roofline": {"bytes_per_token_avg": step_bytes / NEW,
+                          "achieved_gbs": step_gbs,
+                          "frac": (step_gbs / peaks["hbm_gbs"]) if step_gbs else None},
+        "cpu_baseline": cpu,
+        "clocks": clk,
+        "gpu_launches": launches_per_token * NEW * args.steps,
+    }
+    print(json.dumps(line), flush=True)
+    return 0
+
+
+def main():
+    ap = argparse.ArgumentParser()
+    ap.add_argument("--gpus", type=int, default=1)
+    ap.add_argument("--steps", type=int, default=20)
+    ap.add_argument("--warmup", type=int, default=3)
+    ap.add_argument("--impl", default="ours", choices=["ours", "reference"])
+    ap.add_argument("--no-cpu-baseline", action="store_true")
+    args = ap.parse_args()
+    if args.impl == "reference":
+        return run_reference(args)
+    return run_ours(args)
+
+
+if __name__ == "__main__":
+    sys.exit(main())

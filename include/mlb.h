@@ -1,0 +1,247 @@
+/*
+ * mini_llama_b200 — C ABI of the B200 (sm_100a) implementation of mini_llama's
+ * decode/prefill hot path.
+ *
+ * Plain pointers, sizes and int status codes; no C++ or torch types.  Every
+ * entry point that replaces a reference interface cites it as
+ * "replaces <reference file>:<lines>" (paths inside the mini_llama project).
+ * The C++17 adapter in mini_llama_b200/adapter/ implements the reference's own
+ * headers (include/cuda_quant.h, cuda_attention.h, cuda_ops.h, cuda_kv_cache.h,
+ * cuda_tensor.h, cuda_data.h) on top of these functions, so the reference's
+ * forward.cpp, loaders and sampler link against this library unchanged.
+ *
+ * Conventions
+ *  - All device pointers belong to `device`.  Unless stated otherwise a call
+ *    only enqueues work on the library stream of that device (see
+ *    mlb_get_stream) and returns; results are visible to later calls of this
+ *    library, to mlb_memcpy_d2h and after mlb_synchronize.
+ *  - Tensors are fp32, row-major.  Quantized weights are GGUF blocks of 32
+ *    elements, rows of ceil(K/32) blocks: Q8_0 {fp16 d; int8 q[32]} (34 B),
+ *    Q4_0 {fp16 d; uint8 q[16]} (18 B, w = d*(q-8), low nibbles are elements
+ *    0-15), Q4_1 {fp16 d; fp16 m; uint8 q[16]} (20 B, w = d*q + m).
+ *  - KV caches are fp32 [n_layers, max_seq_len, n_kv_heads, head_dim].
+ *  - On failure a call returns a nonzero mlb_status and mlb_last_error()
+ *    returns the message (thread-local), prefixed with the caller's name the
+ *    way the reference's exceptions are.
+ */
+#ifndef MINI_LLAMA_B200_MLB_H
+#define MINI_LLAMA_B200_MLB_H
+
+#include <stddef.h>
+#include <stdint.h>
+
+#ifdef __cplusplus
+extern "C" {
+#endif
+
+#define MLB_ABI_VERSION 1
+
+typedef enum {
+    MLB_OK = 0,
+    MLB_ERR_INVALID_ARGUMENT = 1, /* the reference throws std::runtime_error */
+    MLB_ERR_OUT_OF_RANGE = 2,     /* the reference throws std::out_of_range */
+    MLB_ERR_CUDA = 3,             /* CUDA runtime error */
+    MLB_ERR_UNSUPPORTED = 4,      /* shape outside what this build supports */
+    MLB_ERR_DEVICE_TIMEOUT = 5    /* a bounded device-side wait expired */
+} mlb_status;
+
+typedef enum { MLB_F32 = 0, MLB_Q8_0 = 1, MLB_Q4_0 = 2, MLB_Q4_1 = 3 } mlb_qtype;
+typedef enum { MLB_ROPE_NORMAL = 0, MLB_ROPE_NEOX = 1 } mlb_rope_type;
+
+const char* mlb_last_error(void);
+int mlb_abi_version(void);
+
+/* ------------------------------------------------------------ device runtime
+ * replaces include/cuda_data.h:16-35 (CheckCudaRuntimeBuilt, GetCudaDeviceCount,
+ * CudaSetDevice, GetCudaDeviceInfo, CudaMallocBytes, CudaFreeBytes,
+ * CudaMemcpyBytes) and the storage of include/cuda_tensor.h:9-58.
+ * mlb_malloc/mlb_free are stream-ordered on the library stream and served from
+ * a per-device pool that keeps freed blocks (no cudaFree in steady state). */
+typedef struct {
+    char name[256];
+    int compute_major;
+    int compute_minor;
+    size_t total_memory_bytes;
+    int sm_count;
+    int driver_version;
+    int runtime_version;
+} mlb_device_info;
+
+int mlb_device_count(int* count);
+int mlb_set_device(int device);
+int mlb_get_device_info(int device, mlb_device_info* info);
+int mlb_get_stream(int device, void** cuda_stream);
+int mlb_malloc(int device, size_t bytes, void** ptr);
+int mlb_free(int device, void* ptr);
+/* host -> device: returns once the host buffer may be reused */
+int mlb_memcpy_h2d(int device, void* dst, const void* src, size_t bytes);
+/* device -> host: waits for prior library work on the device, then copies */
+int mlb_memcpy_d2h(int device, void* dst, const void* src, size_t bytes);
+int mlb_memcpy_d2d(int device, void* dst, const void* src, size_t bytes);
+int mlb_memset(int device, void* dst, int value, size_t bytes);
+int mlb_synchronize(int device);
+
+/* ------------------------------------------------------------ quantized linear
+ * y[rows, out] = x[rows, in] . dequant(W[out, in])^T (+ bias[out])
+ * replaces include/cuda_quant.h:13-38 (CudaQ80/Q40/Q41 Linear, ...DeviceWeight,
+ * ...DeviceInput), reference kernels src/cuda_quant.cu:40-135.
+ * block_count must equal out * ceil(in/32) (the reference's check,
+ * src/cuda_quant.cu:175-181).  bias may be NULL.  rows <= 8 runs the
+ * bandwidth-bound bulk-copy GEMV; larger batches use the tensor-core path
+ * when available. */
+int mlb_q80_linear(int device, const float* x, const void* w, size_t block_count, int rows,
+                   int in_features, int out_features, const float* bias, float* y);
+int mlb_q40_linear(int device, const float* x, const void* w, size_t block_count, int rows,
+                   int in_features, int out_features, const float* bias, float* y);
+int mlb_q41_linear(int device, const float* x, const void* w, size_t block_count, int rows,
+                   int in_features, int out_features, const float* bias, float* y);
+/* Same with the block type as an argument (MLB_Q8_0 / MLB_Q4_0 / MLB_Q4_1). */
+int mlb_quant_linear(int device, int qtype, const float* x, const void* w, size_t block_count,
+                     int rows, int in_features, int out_features, const float* bias, float* y);
+
+/* ------------------------------------------------------------ quantization
+ * Device quantizer, bit-identical to the reference's QuantizeToQ80 and
+ * QuantizeToQ40 (src/quant.cpp:104-240, fp16 rounding of src/quant.cpp:17-52)
+ * and, for Q4_1, to the reference GPU test's quantizer
+ * (test/gpu_core_test.cpp:156-198).  replaces the host-side
+ * QuantizeModelToQ80/Q40 (src/model.cpp:454-493) for weights already in HBM.
+ * mlb_dequantize replaces DeQuantizeFromQ80/Q40, DequantizeFromQ41
+ * (src/quant.cpp:153-317). */
+int mlb_quantize(int device, int qtype, const float* x, int rows, int cols, void* blocks);
+int mlb_dequantize(int device, int qtype, const void* blocks, int rows, int cols, float* y);
+
+/* ------------------------------------------------------------ element-wise ops
+ * replaces include/cuda_ops.h:11-46, reference kernels src/cuda_ops.cu:22-172 */
+int mlb_rmsnorm(int device, const float* x, const float* weight, int n, float eps, float* y);
+/* RoPE in place on q [n_heads, head_dim] and k [n_kv_heads, head_dim] at
+ * position pos.  The rotation angles are the reference CPU's table values
+ * (src/context.cpp:16-25: freq = 1/powf(theta, 2i/head_dim), angle = pos*freq)
+ * computed on the host; rope_type MLB_ROPE_NORMAL pairs (2i, 2i+1),
+ * MLB_ROPE_NEOX pairs (i, i + head_dim/2) (src/ops.cpp:123-168). */
+int mlb_rope(int device, float* q, float* k, int n_heads, int n_kv_heads, int head_dim, int pos,
+             float theta, int rope_type);
+int mlb_silu(int device, const float* x, size_t n, float* y);
+int mlb_mul(int device, const float* a, const float* b, size_t n, float* y);
+int mlb_add(int device, const float* a, const float* b, size_t n, float* y);
+int mlb_softmax(int device, const float* x, int n, float* y);
+int mlb_embedding(int device, const float* table, int vocab_size, int dim, int token, float* y);
+/* Index of the first maximum of x[n] (src/ops.cpp:199-212), written to the
+ * device int at out_index. */
+int mlb_argmax(int device, const float* x, int n, int* out_index);
+
+/* ------------------------------------------------------------ KV cache
+ * replaces CudaKVCache::WriteDevice (src/cuda_kv_cache.cpp:157-182): k and v
+ * [n_kv_heads, head_dim] written at (layer, pos) of both caches by one kernel. */
+int mlb_kv_write(int device, float* key_cache, float* value_cache, int n_layers,
+                 int max_seq_len, int n_kv_heads, int head_dim, int layer, int pos,
+                 const float* k, const float* v);
+
+/* ------------------------------------------------------------ decode attention
+ * out[n_heads, head_dim] = softmax(q . K[0..pos]^T / sqrt(head_dim)) . V[0..pos]
+ * for query head h reading KV head h / (n_heads / n_kv_heads).
+ * replaces include/cuda_attention.h:10-14 (CudaAttentionDecode,
+ * CudaAttentionDecodeDeviceInputs), reference kernels
+ * src/cuda_attention.cu:87-181.  Split-K over positions with a merged partial
+ * softmax; scratch comes from the library's per-device workspace. */
+int mlb_attention_decode(int device, const float* q, const float* key_cache,
+                         const float* value_cache, int n_layers, int max_seq_len, int layer,
+                         int pos, int n_heads, int n_kv_heads, int head_dim, float* out);
+/* Batch of independent sequences: q [batch, n_heads, head_dim], caches
+ * [batch, n_layers, max_seq_len, n_kv_heads, head_dim], positions[batch] a
+ * device int array (each sequence attends to 0..positions[b]), out
+ * [batch, n_heads, head_dim].  No reference counterpart: the reference decodes
+ * one sequence per call; this is the batched form of the same computation. */
+int mlb_attention_decode_batched(int device, int batch, const float* q, const float* key_cache,
+                                 const float* value_cache, int n_layers, int max_seq_len,
+                                 int layer, const int* positions, int max_pos, int n_heads,
+                                 int n_kv_heads, int head_dim, float* out);
+
+/* ------------------------------------------------------------ synthetic inputs
+ * Seeded N(0, sigma) fill on the device, bit-identical to the host generator
+ * used for fixtures (splitmix64 counter stream, Irwin-Hall sum of 12 uniform
+ * 32-bit integers).  No reference counterpart (test and benchmark inputs). */
+int mlb_synth_normal(int device, float* out, size_t n, uint64_t seed, uint64_t stream,
+                     double sigma);
+
+/* ------------------------------------------------------------ decode session
+ * The whole-token device path: replaces the device branch of ForwardToken /
+ * ForwardBatch (src/forward.cpp:292-333, :642-684) together with the greedy
+ * GetArgMax of the sampler (src/ops.cpp:199-212, src/sampler.cpp:141-151).
+ * One token = embedding, n_layers x (RMSNorm+QKV+bias, RoPE+KV write+split-K
+ * attention, O-proj+residual, RMSNorm+gate/up+SwiGLU, down+residual), final
+ * RMSNorm, lm_head, argmax, captured once as a CUDA graph whose position and
+ * token live in device memory. */
+typedef struct {
+    int vocab_size;
+    int dim;
+    int hidden_dim;
+    int n_layers;
+    int n_heads;
+    int n_kv_heads;
+    int head_dim;
+    int max_seq_len;
+    float rope_theta;
+    float rms_norm_eps;
+    int rope_type;   /* mlb_rope_type */
+    int weight_type; /* mlb_qtype of every linear weight (lm_head included) */
+    int qkv_bias;    /* 1 when bq/bk/bv are present (Qwen2) */
+} mlb_model_config; /* mirrors ModelConfig, include/model.h:16-28 */
+
+typedef enum {
+    MLB_W_EMBEDDING = 0, /* [vocab, dim] f32 */
+    MLB_W_FINAL_NORM = 1,
+    MLB_W_LM_HEAD = 2, /* [vocab, dim] weight_type */
+    MLB_W_ATTN_NORM = 3,
+    MLB_W_WQ = 4,
+    MLB_W_WK = 5,
+    MLB_W_WV = 6,
+    MLB_W_BQ = 7,
+    MLB_W_BK = 8,
+    MLB_W_BV = 9,
+    MLB_W_WO = 10,
+    MLB_W_FFN_NORM = 11,
+    MLB_W_GATE = 12,
+    MLB_W_UP = 13,
+    MLB_W_DOWN = 14
+} mlb_weight_kind; /* the weight names of UploadModelWeightsToCuda, src/model.cpp:255-286 */
+
+typedef struct mlb_model mlb_model;
+typedef struct mlb_session mlb_session;
+
+int mlb_model_create(int device, const mlb_model_config* config, mlb_model** model);
+int mlb_model_destroy(mlb_model* model);
+/* Device storage of one weight (allocated by the model); bytes is its size. */
+int mlb_model_weight(mlb_model* model, int layer, int kind, void** dev_ptr, size_t* bytes);
+/* Copies a weight from host (src_is_host = 1) or device memory. */
+int mlb_model_set_weight(mlb_model* model, int layer, int kind, const void* src, size_t bytes,
+                         int src_is_host);
+/* Total bytes of device weight storage. */
+int mlb_model_bytes(mlb_model* model, size_t* bytes);
+
+int mlb_session_create(mlb_model* model, mlb_session** session);
+int mlb_session_destroy(mlb_session* session);
+/* Clears the KV cache (CudaKVCache::Clear, src/cuda_kv_cache.cpp:39-51). */
+int mlb_session_reset(mlb_session* session);
+/* ForwardToken: one token at position pos.  logits (host, vocab floats) and
+ * next_token (host) may each be NULL. */
+int mlb_session_forward(mlb_session* session, int token, int pos, float* logits,
+                        int* next_token);
+/* Greedy generation: forwards the prompt (host ids) at positions
+ * start_pos.., then n_new greedy tokens (host out_tokens[n_new]); tokens are
+ * fed back on the device. */
+int mlb_session_generate(mlb_session* session, const int* prompt, int n_prompt, int start_pos,
+                         int n_new, int* out_tokens);
+/* Device-resident greedy decode for measurement: tokens (device int array of
+ * n_steps + 1) holds the start token in tokens[0]; step i forwards tokens[i]
+ * at position start_pos + i and writes the argmax to tokens[i + 1].  Enqueued
+ * only; no host synchronisation. */
+int mlb_session_decode_device(mlb_session* session, int* tokens, int start_pos, int n_steps);
+/* Device pointer of the last logits (vocab floats). */
+int mlb_session_logits(mlb_session* session, const float** logits);
+/* Device pointers of the session KV cache. */
+int mlb_session_kv_cache(mlb_session* session, float** key_cache, float** value_cache);
+
+#ifdef __cplusplus
+}
+#endif
+#endif

@@ -1,0 +1,122 @@
+// Decode-attention entry points (replace mini_llama include/cuda_attention.h:10-14).
+#include <cmath>
+
+#include "attention.cuh"
+
+namespace mlb {
+
+int AttnChunks(int max_npos, int batch, int n_kv, int hgroups, int sm_count) {
+    // ~128 positions per CTA (one 32-position tile per warp), but no more CTAs
+    // than about four waves of the SMs.
+    long long base = 1LL * batch * n_kv * hgroups;
+    long long by_len = (max_npos + 127) / 128;
+    long long by_sms = std::max(1LL, (4LL * sm_count + base - 1) / base);
+    long long c = std::min(by_len, by_sms);
+    return static_cast<int>(std::max(1LL, std::min(c, 1024LL)));
+}
+
+template <int DPL>
+void LaunchAttnT(const AttnParams& p, int batch, cudaStream_t stream, bool pdl) {
+    const size_t smem = AttnSmemBytes(p.hd);
+    static int configured[64] = {};
+    int dev = 0;
+    CheckCuda(cudaGetDevice(&dev), "cudaGetDevice");
+    if (dev >= 64 || configured[dev] < static_cast<int>(smem)) {
+        CheckCuda(cudaFuncSetAttribute(AttnSplitKernel<DPL>,
+                                       cudaFuncAttributeMaxDynamicSharedMemorySize,
+                                       static_cast<int>(smem)),
+                  "cudaFuncSetAttribute(AttnSplitKernel)");
+        if (dev < 64) configured[dev] = static_cast<int>(smem);
+    }
+    dim3 grid(p.n_kv * p.hgroups, p.chunks, batch);
+    Launch("AttnSplitKernel", AttnSplitKernel<DPL>, grid, dim3(kAttnThreads), smem, stream, pdl, p);
+}
+
+void LaunchAttention(const AttnParams& p, int batch, cudaStream_t stream, bool pdl) {
+    const int dpl = (p.hd + 31) / 32;
+    if (dpl <= 1) return LaunchAttnT<1>(p, batch, stream, pdl);
+    if (dpl <= 2) return LaunchAttnT<2>(p, batch, stream, pdl);
+    if (dpl <= 4) return LaunchAttnT<4>(p, batch, stream, pdl);
+    if (dpl <= 8) return LaunchAttnT<8>(p, batch, stream, pdl);
+    Fail(MLB_ERR_UNSUPPORTED, "attention: head_dim above 256 is not supported");
+}
+
+namespace {
+
+void AttentionDecode(const char* caller, int device, int batch, const float* q, const float* kc,
+                     const float* vc, int n_layers, int max_seq_len, int layer,
+                     const int* positions, int pos, int n_heads, int n_kv_heads, int head_dim,
+                     float* out) {
+    Require(q && kc && vc && out, caller, "CUDA KV cache is empty");
+    Require(batch > 0, caller, "batch must be positive");
+    Require(n_layers > 0 && max_seq_len > 0, caller, "cache shape must be positive");
+    Require(layer >= 0 && layer < n_layers, caller, "layer out of range", MLB_ERR_OUT_OF_RANGE);
+    Require(pos >= 0 && pos < max_seq_len, caller, "position out of range", MLB_ERR_OUT_OF_RANGE);
+    Require(n_heads > 0 && n_kv_heads > 0 && head_dim > 0, caller,
+            "head counts and head_dim must be positive");
+    Require(n_heads % n_kv_heads == 0, caller, "n_heads must be divisible by n_kv_heads");
+    Require(head_dim <= 256, caller, "head_dim above 256 is not supported", MLB_ERR_UNSUPPORTED);
+    DeviceContext& c = Ctx(device);
+    AttnParams p = {};
+    p.q = q;
+    p.q_batch_stride = size_t(n_heads) * head_dim;
+    p.kc = const_cast<float*>(kc);
+    p.vc = const_cast<float*>(vc);
+    p.seq_stride = size_t(n_layers) * max_seq_len * n_kv_heads * head_dim;
+    p.layer = layer;
+    p.max_seq_len = max_seq_len;
+    p.n_heads = n_heads;
+    p.n_kv = n_kv_heads;
+    p.hd = head_dim;
+    p.group = n_heads / n_kv_heads;
+    p.hgroups = (p.group + kAttnGmax - 1) / kAttnGmax;
+    p.scale = 1.0f / std::sqrt(static_cast<float>(head_dim));
+    p.pos_dev = positions;
+    p.pos_stride = positions ? 1 : 0;
+    p.pos_host = pos;
+    p.chunks = AttnChunks(pos + 1, batch, n_kv_heads, p.hgroups, c.sm_count);
+    p.out = out;
+    if (p.chunks > 1) {
+        const size_t rows = size_t(batch) * n_heads * p.chunks;
+        float* ws = static_cast<float*>(Workspace(c, rows * (head_dim + 2) * sizeof(float)));
+        p.part_ml = ws;
+        p.part_o = ws + rows * 2;
+    }
+    LaunchAttention(p, batch, c.stream, false);
+    if (p.chunks > 1) {
+        AttnMergeKernel<<<batch * n_heads, 128, 0, c.stream>>>(p.part_ml, p.part_o, p.chunks,
+                                                               head_dim, out);
+        CheckCuda(cudaGetLastError(), "AttnMergeKernel");
+    }
+}
+
+}  // namespace
+}  // namespace mlb
+
+using namespace mlb;
+
+extern "C" {
+
+int mlb_attention_decode(int device, const float* q, const float* key_cache,
+                         const float* value_cache, int n_layers, int max_seq_len, int layer,
+                         int pos, int n_heads, int n_kv_heads, int head_dim, float* out) {
+    return Guard([&] {
+        AttentionDecode("CudaAttentionDecodeDeviceInput", device, 1, q, key_cache, value_cache,
+                        n_layers, max_seq_len, layer, nullptr, pos, n_heads, n_kv_heads,
+                        head_dim, out);
+    });
+}
+
+int mlb_attention_decode_batched(int device, int batch, const float* q, const float* key_cache,
+                                 const float* value_cache, int n_layers, int max_seq_len,
+                                 int layer, const int* positions, int max_pos, int n_heads,
+                                 int n_kv_heads, int head_dim, float* out) {
+    return Guard([&] {
+        Require(positions != nullptr, "mlb_attention_decode_batched", "positions is null");
+        AttentionDecode("mlb_attention_decode_batched", device, batch, q, key_cache, value_cache,
+                        n_layers, max_seq_len, layer, positions, max_pos, n_heads, n_kv_heads,
+                        head_dim, out);
+    });
+}
+
+}  // extern "C"

@@ -1,0 +1,589 @@
+// Decode session: the whole-token device path of mini_llama (device branch of
+// ForwardToken, src/forward.cpp:292-333 and :642-666, plus the greedy GetArgMax
+// of src/ops.cpp:199-212) as one CUDA graph per token.
+//
+// Per layer the graph holds five kernels, each a fused step:
+//   1. RMSNorm(x) -> [wq|wk|wv] GEMV + bias                      -> qkv
+//   2. RoPE(q, k) from the reference CPU tables, KV-cache write,
+//      split-K GQA attention                                      -> partials
+//   3. merge partials -> wo GEMV + residual                        -> x_mid
+//   4. RMSNorm(x_mid) -> [gate|up] GEMV -> SwiGLU                  -> ff
+//   5. down GEMV + residual                                        -> x
+// then RMSNorm -> lm_head GEMV -> arg-max (token and position stay on the
+// device).  Kernels are launched with programmatic dependent launch, so each
+// one streams its weights into shared memory while the previous one finishes.
+#include <array>
+#include <climits>
+#include <cmath>
+#include <memory>
+#include <vector>
+
+#include "attention.cuh"
+#include "qgemv.cuh"
+
+namespace mlb {
+
+namespace {
+
+constexpr int kKinds = 15;
+constexpr int kRingBudget = 96 * 1024;
+
+// x = embedding[hist[pos]]; an out-of-range token sets the status flag and
+// leaves zeros rather than reading outside the table.
+__global__ void DecodeEmbedKernel(const float* table, int vocab, int dim, const int* hist,
+                                  const int* pos, float* x, int* status) {
+    GridDepWait();
+    GridDepLaunch();
+    const int tok = hist[*pos];
+    const bool ok = tok >= 0 && tok < vocab;
+    if (!ok && threadIdx.x == 0 && blockIdx.x == 0) atomicExch(status, MLB_ERR_OUT_OF_RANGE);
+    const float* row = table + size_t(ok ? tok : 0) * dim;
+    for (int i = blockIdx.x * blockDim.x + threadIdx.x; i < dim; i += gridDim.x * blockDim.x)
+        x[i] = ok ? row[i] : 0.0f;
+}
+
+size_t Align256(size_t v) { return (v + 255) & ~size_t(255); }
+
+size_t LinearBytes(int qtype, int rows, int cols) {
+    return size_t(rows) * ((cols + 31) / 32) * BlockBytes(qtype);
+}
+
+}  // namespace
+}  // namespace mlb
+
+struct mlb_model {
+    int device = 0;
+    mlb_model_config cfg = {};
+    void* arena = nullptr;
+    size_t arena_bytes = 0;
+    struct Slot {
+        size_t offset = 0;
+        size_t bytes = 0;
+    };
+    Slot global[3];                        // embedding, final_norm, lm_head
+    std::vector<std::array<Slot, 15>> layer;  // per layer, kinds 3..14
+    float* rope_cos = nullptr;
+    float* rope_sin = nullptr;
+
+    void* Ptr(const Slot& s) const { return s.bytes ? static_cast<char*>(arena) + s.offset : nullptr; }
+    const Slot& Get(int l, int kind) const {
+        return kind < 3 ? global[kind] : layer[l][kind];
+    }
+};
+
+struct mlb_session {
+    mlb_model* model = nullptr;
+    float* kc = nullptr;
+    float* vc = nullptr;
+    float* x = nullptr;
+    float* xmid = nullptr;
+    float* qkv = nullptr;
+    float* attn = nullptr;
+    float* ff = nullptr;
+    float* logits = nullptr;
+    float* part_ml = nullptr;
+    float* part_o = nullptr;
+    float* am_val = nullptr;
+    int* am_idx = nullptr;
+    unsigned* am_counter = nullptr;
+    int* state = nullptr;  // [0] pos, [1] gen_from, [2] next token, [3] status
+    int* hist = nullptr;   // [max_seq_len + 1]
+    int chunks = 1;
+    size_t cache_floats = 0;
+    cudaGraph_t graph = nullptr;
+    cudaGraphExec_t exec = nullptr;
+    std::vector<void*> allocations;
+};
+
+namespace mlb {
+namespace {
+
+void* DevAlloc(mlb_session* s, DeviceContext& c, size_t bytes) {
+    void* p = nullptr;
+    CheckCuda(cudaMallocFromPoolAsync(&p, bytes, c.pool, c.stream), "cudaMallocFromPoolAsync");
+    s->allocations.push_back(p);
+    return p;
+}
+
+void ValidateConfig(const mlb_model_config& c) {
+    const char* w = "mlb_model_create";
+    Require(c.vocab_size > 0 && c.dim > 0 && c.hidden_dim > 0 && c.n_layers > 0, w,
+            "model dimensions must be positive");
+    Require(c.n_heads > 0 && c.n_kv_heads > 0 && c.head_dim > 0 && c.max_seq_len > 0, w,
+            "head shape must be positive");
+    Require(c.n_heads % c.n_kv_heads == 0, w, "n_heads must be divisible by n_kv_heads");
+    Require(c.head_dim % 2 == 0, w, "head_dim must be positive and even");
+    Require(c.head_dim <= 256, w, "head_dim above 256 is not supported", MLB_ERR_UNSUPPORTED);
+    Require(c.weight_type == MLB_Q8_0 || c.weight_type == MLB_Q4_0 || c.weight_type == MLB_Q4_1, w,
+            "weight_type must be Q8_0, Q4_0 or Q4_1");
+    Require(std::isfinite(c.rms_norm_eps) && c.rms_norm_eps > 0.0f, w,
+            "eps must be positive and finite");
+    Require(std::isfinite(c.rope_theta) && c.rope_theta > 0.0f, w, "theta must be positive");
+}
+
+size_t KindBytes(const mlb_model_config& c, int kind) {
+    const int qd = c.n_heads * c.head_dim, kd = c.n_kv_heads * c.head_dim;
+    const int qt = c.weight_type;
+    switch (kind) {
+        case MLB_W_EMBEDDING: return size_t(c.vocab_size) * c.dim * 4;
+        case MLB_W_FINAL_NORM: return size_t(c.dim) * 4;
+        case MLB_W_LM_HEAD: return LinearBytes(qt, c.vocab_size, c.dim);
+        case MLB_W_ATTN_NORM: return size_t(c.dim) * 4;
+        case MLB_W_WQ: return LinearBytes(qt, qd, c.dim);
+        case MLB_W_WK: return LinearBytes(qt, kd, c.dim);
+        case MLB_W_WV: return LinearBytes(qt, kd, c.dim);
+        case MLB_W_BQ: return c.qkv_bias ? size_t(qd) * 4 : 0;
+        case MLB_W_BK: return c.qkv_bias ? size_t(kd) * 4 : 0;
+        case MLB_W_BV: return c.qkv_bias ? size_t(kd) * 4 : 0;
+        case MLB_W_WO: return LinearBytes(qt, c.dim, qd);
+        case MLB_W_FFN_NORM: return size_t(c.dim) * 4;
+        case MLB_W_GATE: return LinearBytes(qt, c.hidden_dim, c.dim);
+        case MLB_W_UP: return LinearBytes(qt, c.hidden_dim, c.dim);
+        case MLB_W_DOWN: return LinearBytes(qt, c.dim, c.hidden_dim);
+    }
+    return 0;
+}
+
+// Captures one token step on the library stream.
+void CaptureStep(mlb_session* s, DeviceContext& c) {
+    mlb_model* m = s->model;
+    const mlb_model_config& cf = m->cfg;
+    const int qt = cf.weight_type;
+    const int qd = cf.n_heads * cf.head_dim, kd = cf.n_kv_heads * cf.head_dim;
+    int* pos = s->state;
+    int* gen_from = s->state + 1;
+    int* next = s->state + 2;
+    int* status = s->state + 3;
+    cudaStream_t st = c.stream;
+
+    CheckCuda(cudaStreamBeginCapture(st, cudaStreamCaptureModeThreadLocal), "cudaStreamBeginCapture");
+    try {
+        Launch("DecodeEmbedKernel", DecodeEmbedKernel, dim3(4), dim3(256), 0, st, true,
+               static_cast<const float*>(m->Ptr(m->global[MLB_W_EMBEDDING])), cf.vocab_size,
+               cf.dim, const_cast<const int*>(s->hist), const_cast<const int*>(pos), s->x, status);
+        for (int l = 0; l < cf.n_layers; ++l) {
+            auto W = [&](int kind) { return static_cast<const uint8_t*>(m->Ptr(m->Get(l, kind))); };
+            auto F = [&](int kind) { return static_cast<const float*>(m->Ptr(m->Get(l, kind))); };
+            // 1. RMSNorm + QKV + bias
+            {
+                GemvParams p = {};
+                p.K = cf.dim;
+                p.nseg = 3;
+                p.seg[0] = GemvSeg{W(MLB_W_WQ), F(MLB_W_BQ), qd, 0, 0, 0};
+                p.seg[1] = GemvSeg{W(MLB_W_WK), F(MLB_W_BK), kd, qd, 0, 0};
+                p.seg[2] = GemvSeg{W(MLB_W_WV), F(MLB_W_BV), kd, qd + kd, 0, 0};
+                p.x = s->x;
+                p.y = s->qkv;
+                p.y_stride = qd + 2 * kd;
+                p.norm_w = F(MLB_W_ATTN_NORM);
+                p.eps = cf.rms_norm_eps;
+                p.status = status;
+                GemvPlan plan = PlanGemv(p, qt, 1, false, c.sm_count, c.max_smem_optin, 1, kRingBudget);
+                Require(plan.ok, "mlb_session", "QKV shape not supported by the GEMV", MLB_ERR_UNSUPPORTED);
+                LaunchGemvDecode(qt, kProRmsNorm, kEpiStore, p, plan, st);
+            }
+            // 2. RoPE + KV write + split-K attention
+            {
+                AttnParams a = {};
+                a.q = s->qkv;
+                a.q_batch_stride = 0;
+                a.kc = s->kc;
+                a.vc = s->vc;
+                a.seq_stride = 0;
+                a.layer = l;
+                a.max_seq_len = cf.max_seq_len;
+                a.n_heads = cf.n_heads;
+                a.n_kv = cf.n_kv_heads;
+                a.hd = cf.head_dim;
+                a.group = cf.n_heads / cf.n_kv_heads;
+                a.hgroups = (a.group + kAttnGmax - 1) / kAttnGmax;
+                a.chunks = s->chunks;
+                a.scale = 1.0f / std::sqrt(static_cast<float>(cf.head_dim));
+                a.pos_dev = pos;
+                a.pos_stride = 0;
+                a.out = s->attn;
+                a.part_ml = s->part_ml;
+                a.part_o = s->part_o;
+                a.fused_rope = 1;
+                a.kv_new = s->qkv + qd;
+                a.rope_cos = m->rope_cos;
+                a.rope_sin = m->rope_sin;
+                a.neox = cf.rope_type == MLB_ROPE_NEOX;
+                LaunchAttention(a, 1, st, true);
+            }
+            // 3. O projection + residual
+            {
+                GemvParams p = {};
+                p.K = qd;
+                p.nseg = 1;
+                p.seg[0] = GemvSeg{W(MLB_W_WO), nullptr, cf.dim, 0, 0, 0};
+                p.x = s->attn;
+                p.y = s->xmid;
+                p.y_stride = cf.dim;
+                p.residual = s->x;
+                p.res_stride = cf.dim;
+                p.part_ml = s->part_ml;
+                p.part_o = s->part_o;
+                p.n_heads = cf.n_heads;
+                p.head_dim = cf.head_dim;
+                p.chunks = s->chunks;
+                p.status = status;
+                GemvPlan plan = PlanGemv(p, qt, 1, false, c.sm_count, c.max_smem_optin, 1, kRingBudget);
+                Require(plan.ok, "mlb_session", "O-projection shape not supported", MLB_ERR_UNSUPPORTED);
+                LaunchGemvDecode(qt, s->chunks > 1 ? kProAttnMerge : kProPlain, kEpiResidual, p,
+                                 plan, st);
+            }
+            // 4. RMSNorm + gate/up + SwiGLU
+            {
+                GemvParams p = {};
+                p.K = cf.dim;
+                p.nseg = 2;
+                p.seg[0] = GemvSeg{W(MLB_W_GATE), nullptr, cf.hidden_dim, 0, 0, 0};
+                p.seg[1] = GemvSeg{W(MLB_W_UP), nullptr, cf.hidden_dim, 0, 0, 0};
+                p.x = s->xmid;
+                p.y = s->ff;
+                p.y_stride = cf.hidden_dim;
+                p.norm_w = F(MLB_W_FFN_NORM);
+                p.eps = cf.rms_norm_eps;
+                p.status = status;
+                GemvPlan plan = PlanGemv(p, qt, 1, true, c.sm_count, c.max_smem_optin, 1, kRingBudget);
+                Require(plan.ok, "mlb_session", "FFN shape not supported", MLB_ERR_UNSUPPORTED);
+                LaunchGemvDecode(qt, kProRmsNorm, kEpiSwiglu, p, plan, st);
+            }
+            // 5. down + residual
+            {
+                GemvParams p = {};
+                p.K = cf.hidden_dim;
+                p.nseg = 1;
+                p.seg[0] = GemvSeg{W(MLB_W_DOWN), nullptr, cf.dim, 0, 0, 0};
+                p.x = s->ff;
+                p.y = s->x;
+                p.y_stride = cf.dim;
+                p.residual = s->xmid;
+                p.res_stride = cf.dim;
+                p.status = status;
+                GemvPlan plan = PlanGemv(p, qt, 1, false, c.sm_count, c.max_smem_optin, 1, kRingBudget);
+                Require(plan.ok, "mlb_session", "down-projection shape not supported", MLB_ERR_UNSUPPORTED);
+                LaunchGemvDecode(qt, kProPlain, kEpiResidual, p, plan, st);
+            }
+        }
+        // final RMSNorm + lm_head + arg-max
+        {
+            GemvParams p = {};
+            p.K = cf.dim;
+            p.nseg = 1;
+            p.seg[0] = GemvSeg{static_cast<const uint8_t*>(m->Ptr(m->global[MLB_W_LM_HEAD])),
+                               nullptr, cf.vocab_size, 0, 0, 0};
+            p.x = s->x;
+            p.y = s->logits;
+            p.y_stride = cf.vocab_size;
+            p.norm_w = static_cast<const float*>(m->Ptr(m->global[MLB_W_FINAL_NORM]));
+            p.eps = cf.rms_norm_eps;
+            p.am_val = s->am_val;
+            p.am_idx = s->am_idx;
+            p.am_counter = s->am_counter;
+            p.am_token = next;
+            p.am_pos = pos;
+            p.am_hist = s->hist;
+            p.am_gen_from = gen_from;
+            p.status = status;
+            GemvPlan plan = PlanGemv(p, qt, 1, false, c.sm_count, c.max_smem_optin, 1, kRingBudget);
+            Require(plan.ok, "mlb_session", "lm_head shape not supported", MLB_ERR_UNSUPPORTED);
+            Require(plan.grid <= 4 * c.sm_count, "mlb_session", "arg-max partial buffer too small");
+            LaunchGemvDecode(qt, kProRmsNorm, kEpiArgmax, p, plan, st);
+        }
+    } catch (...) {
+        cudaGraph_t g = nullptr;
+        cudaStreamEndCapture(st, &g);
+        if (g) cudaGraphDestroy(g);
+        throw;
+    }
+    CheckCuda(cudaStreamEndCapture(st, &s->graph), "cudaStreamEndCapture");
+    CheckCuda(cudaGraphInstantiate(&s->exec, s->graph, 0), "cudaGraphInstantiate");
+}
+
+void CheckStatus(mlb_session* s, DeviceContext& c) {
+    int status = 0;
+    CheckCuda(cudaMemcpyAsync(&status, s->state + 3, sizeof(int), cudaMemcpyDeviceToHost, c.stream),
+              "cudaMemcpyAsync(status)");
+    CheckCuda(cudaStreamSynchronize(c.stream), "cudaStreamSynchronize");
+    if (status != 0) {
+        CheckCuda(cudaMemsetAsync(s->state + 3, 0, sizeof(int), c.stream), "cudaMemsetAsync");
+        Fail(status, status == MLB_ERR_DEVICE_TIMEOUT
+                         ? "mlb_session: a bounded device wait expired"
+                         : "mlb_session: token id out of range on the device");
+    }
+}
+
+void SetState(mlb_session* s, DeviceContext& c, int pos, int gen_from) {
+    int* h = static_cast<int*>(PinnedStaging(c, 16));
+    CheckCuda(cudaStreamSynchronize(c.stream), "cudaStreamSynchronize");
+    h[0] = pos;
+    h[1] = gen_from;
+    CheckCuda(cudaMemcpyAsync(s->state, h, 2 * sizeof(int), cudaMemcpyHostToDevice, c.stream),
+              "cudaMemcpyAsync(state)");
+}
+
+}  // namespace
+}  // namespace mlb
+
+using namespace mlb;
+
+extern "C" {
+
+int mlb_model_create(int device, const mlb_model_config* config, mlb_model** model) {
+    return Guard([&] {
+        Require(config && model, "mlb_model_create", "null argument");
+        *model = nullptr;
+        ValidateConfig(*config);
+        DeviceContext& c = Ctx(device);
+        auto m = std::make_unique<mlb_model>();
+        m->device = device;
+        m->cfg = *config;
+        size_t off = 0;
+        for (int k = 0; k < 3; ++k) {
+            m->global[k].offset = off;
+            m->global[k].bytes = KindBytes(*config, k);
+            off += Align256(m->global[k].bytes);
+        }
+        m->layer.resize(config->n_layers);
+        for (int l = 0; l < config->n_layers; ++l)
+            for (int k = MLB_W_ATTN_NORM; k < kKinds; ++k) {
+                m->layer[l][k].offset = off;
+                m->layer[l][k].bytes = KindBytes(*config, k);
+                off += Align256(m->layer[l][k].bytes);
+            }
+        const int half = config->head_dim / 2;
+        const size_t table = size_t(config->max_seq_len) * half * 4;
+        m->arena_bytes = off + 2 * Align256(table);
+        CheckCuda(cudaMallocAsync(&m->arena, m->arena_bytes, c.stream), "cudaMallocAsync(weights)");
+        CheckCuda(cudaMemsetAsync(m->arena, 0, m->arena_bytes, c.stream), "cudaMemsetAsync(weights)");
+        m->rope_cos = reinterpret_cast<float*>(static_cast<char*>(m->arena) + off);
+        m->rope_sin = reinterpret_cast<float*>(static_cast<char*>(m->arena) + off + Align256(table));
+        // RoPE tables exactly as the reference CPU builds them (src/context.cpp:16-25)
+        std::vector<float> cs(size_t(config->max_seq_len) * half), sn(cs.size());
+        for (int pos = 0; pos < config->max_seq_len; ++pos)
+            for (int i = 0; i < half; ++i) {
+                float freq = 1.0f / std::pow(config->rope_theta,
+                                             static_cast<float>(2 * i) / static_cast<float>(config->head_dim));
+                cs[size_t(pos) * half + i] = std::cos(static_cast<float>(pos) * freq);
+                sn[size_t(pos) * half + i] = std::sin(static_cast<float>(pos) * freq);
+            }
+        CheckCuda(cudaMemcpyAsync(m->rope_cos, cs.data(), table, cudaMemcpyHostToDevice, c.stream),
+                  "cudaMemcpyAsync(rope)");
+        CheckCuda(cudaMemcpyAsync(m->rope_sin, sn.data(), table, cudaMemcpyHostToDevice, c.stream),
+                  "cudaMemcpyAsync(rope)");
+        CheckCuda(cudaStreamSynchronize(c.stream), "cudaStreamSynchronize");
+        *model = m.release();
+    });
+}
+
+int mlb_model_destroy(mlb_model* model) {
+    return Guard([&] {
+        if (!model) return;
+        DeviceContext& c = Ctx(model->device);
+        CheckCuda(cudaStreamSynchronize(c.stream), "cudaStreamSynchronize");
+        if (model->arena) CheckCuda(cudaFreeAsync(model->arena, c.stream), "cudaFreeAsync");
+        delete model;
+    });
+}
+
+int mlb_model_weight(mlb_model* model, int layer, int kind, void** dev_ptr, size_t* bytes) {
+    return Guard([&] {
+        Require(model && dev_ptr && bytes, "mlb_model_weight", "null argument");
+        Require(kind >= 0 && kind < kKinds, "mlb_model_weight", "unknown weight kind");
+        if (kind >= MLB_W_ATTN_NORM)
+            Require(layer >= 0 && layer < model->cfg.n_layers, "mlb_model_weight",
+                    "layer out of range", MLB_ERR_OUT_OF_RANGE);
+        const auto& slot = model->Get(layer, kind);
+        *dev_ptr = model->Ptr(slot);
+        *bytes = slot.bytes;
+    });
+}
+
+int mlb_model_set_weight(mlb_model* model, int layer, int kind, const void* src, size_t bytes,
+                         int src_is_host) {
+    return Guard([&] {
+        Require(model && src, "mlb_model_set_weight", "null argument");
+        Require(kind >= 0 && kind < kKinds, "mlb_model_set_weight", "unknown weight kind");
+        if (kind >= MLB_W_ATTN_NORM)
+            Require(layer >= 0 && layer < model->cfg.n_layers, "mlb_model_set_weight",
+                    "layer out of range", MLB_ERR_OUT_OF_RANGE);
+        const auto& slot = model->Get(layer, kind);
+        Require(bytes == slot.bytes, "mlb_model_set_weight",
+                "weight shape is not match: expected " + std::to_string(slot.bytes) +
+                    " bytes, got " + std::to_string(bytes));
+        DeviceContext& c = Ctx(model->device);
+        CheckCuda(cudaMemcpyAsync(model->Ptr(slot), src, bytes,
+                                  src_is_host ? cudaMemcpyHostToDevice : cudaMemcpyDeviceToDevice,
+                                  c.stream),
+                  "cudaMemcpyAsync(weight)");
+        if (src_is_host) CheckCuda(cudaStreamSynchronize(c.stream), "cudaStreamSynchronize");
+    });
+}
+
+int mlb_model_bytes(mlb_model* model, size_t* bytes) {
+    return Guard([&] {
+        Require(model && bytes, "mlb_model_bytes", "null argument");
+        *bytes = model->arena_bytes;
+    });
+}
+
+int mlb_session_create(mlb_model* model, mlb_session** session) {
+    return Guard([&] {
+        Require(model && session, "mlb_session_create", "null argument");
+        *session = nullptr;
+        DeviceContext& c = Ctx(model->device);
+        const mlb_model_config& cf = model->cfg;
+        auto s = std::make_unique<mlb_session>();
+        s->model = model;
+        const int qd = cf.n_heads * cf.head_dim, kd = cf.n_kv_heads * cf.head_dim;
+        s->cache_floats = size_t(cf.n_layers) * cf.max_seq_len * kd;
+        const int hgroups = (cf.n_heads / cf.n_kv_heads + kAttnGmax - 1) / kAttnGmax;
+        s->chunks = AttnChunks(cf.max_seq_len, 1, cf.n_kv_heads, hgroups, c.sm_count);
+        s->kc = static_cast<float*>(DevAlloc(s.get(), c, s->cache_floats * 4));
+        s->vc = static_cast<float*>(DevAlloc(s.get(), c, s->cache_floats * 4));
+        s->x = static_cast<float*>(DevAlloc(s.get(), c, size_t(cf.dim) * 4));
+        s->xmid = static_cast<float*>(DevAlloc(s.get(), c, size_t(cf.dim) * 4));
+        s->qkv = static_cast<float*>(DevAlloc(s.get(), c, size_t(qd + 2 * kd) * 4));
+        s->attn = static_cast<float*>(DevAlloc(s.get(), c, size_t(qd) * 4));
+        s->ff = static_cast<float*>(DevAlloc(s.get(), c, size_t(cf.hidden_dim) * 4));
+        s->logits = static_cast<float*>(DevAlloc(s.get(), c, size_t(cf.vocab_size) * 4));
+        const size_t prow = size_t(cf.n_heads) * s->chunks;
+        s->part_ml = static_cast<float*>(DevAlloc(s.get(), c, prow * 2 * 4));
+        s->part_o = static_cast<float*>(DevAlloc(s.get(), c, prow * cf.head_dim * 4));
+        s->am_val = static_cast<float*>(DevAlloc(s.get(), c, size_t(4) * c.sm_count * 4));
+        s->am_idx = static_cast<int*>(DevAlloc(s.get(), c, size_t(4) * c.sm_count * 4));
+        s->am_counter = static_cast<unsigned*>(DevAlloc(s.get(), c, 256));
+        s->state = static_cast<int*>(DevAlloc(s.get(), c, 256));
+        s->hist = static_cast<int*>(DevAlloc(s.get(), c, size_t(cf.max_seq_len + 1) * 4));
+        CheckCuda(cudaMemsetAsync(s->kc, 0, s->cache_floats * 4, c.stream), "cudaMemsetAsync");
+        CheckCuda(cudaMemsetAsync(s->vc, 0, s->cache_floats * 4, c.stream), "cudaMemsetAsync");
+        CheckCuda(cudaMemsetAsync(s->am_counter, 0, 256, c.stream), "cudaMemsetAsync");
+        CheckCuda(cudaMemsetAsync(s->state, 0, 256, c.stream), "cudaMemsetAsync");
+        CheckCuda(cudaMemsetAsync(s->hist, 0, size_t(cf.max_seq_len + 1) * 4, c.stream),
+                  "cudaMemsetAsync");
+        CheckCuda(cudaStreamSynchronize(c.stream), "cudaStreamSynchronize");
+        CaptureStep(s.get(), c);
+        *session = s.release();
+    });
+}
+
+int mlb_session_destroy(mlb_session* session) {
+    return Guard([&] {
+        if (!session) return;
+        DeviceContext& c = Ctx(session->model->device);
+        CheckCuda(cudaStreamSynchronize(c.stream), "cudaStreamSynchronize");
+        if (session->exec) cudaGraphExecDestroy(session->exec);
+        if (session->graph) cudaGraphDestroy(session->graph);
+        for (void* p : session->allocations) CheckCuda(cudaFreeAsync(p, c.stream), "cudaFreeAsync");
+        delete session;
+    });
+}
+
+int mlb_session_reset(mlb_session* session) {
+    return Guard([&] {
+        Require(session != nullptr, "mlb_session_reset", "null session");
+        DeviceContext& c = Ctx(session->model->device);
+        CheckCuda(cudaMemsetAsync(session->kc, 0, session->cache_floats * 4, c.stream), "cudaMemsetAsync");
+        CheckCuda(cudaMemsetAsync(session->vc, 0, session->cache_floats * 4, c.stream), "cudaMemsetAsync");
+    });
+}
+
+int mlb_session_forward(mlb_session* session, int token, int pos, float* logits, int* next_token) {
+    return Guard([&] {
+        Require(session != nullptr, "ForwardToken", "null session");
+        const mlb_model_config& cf = session->model->cfg;
+        Require(token >= 0 && token < cf.vocab_size, "ForwardToken", "token id out of range",
+                MLB_ERR_OUT_OF_RANGE);
+        Require(pos >= 0 && pos < cf.max_seq_len, "ForwardToken", "position out of range",
+                MLB_ERR_OUT_OF_RANGE);
+        DeviceContext& c = Ctx(session->model->device);
+        int* h = static_cast<int*>(PinnedStaging(c, 16));
+        CheckCuda(cudaStreamSynchronize(c.stream), "cudaStreamSynchronize");
+        h[0] = pos;
+        h[1] = INT_MAX;
+        h[2] = token;
+        CheckCuda(cudaMemcpyAsync(session->state, h, 2 * sizeof(int), cudaMemcpyHostToDevice, c.stream),
+                  "cudaMemcpyAsync(state)");
+        CheckCuda(cudaMemcpyAsync(session->hist + pos, h + 2, sizeof(int), cudaMemcpyHostToDevice,
+                                  c.stream),
+                  "cudaMemcpyAsync(token)");
+        CheckCuda(cudaGraphLaunch(session->exec, c.stream), "cudaGraphLaunch");
+        if (logits)
+            CheckCuda(cudaMemcpyAsync(logits, session->logits, size_t(cf.vocab_size) * 4,
+                                      cudaMemcpyDeviceToHost, c.stream),
+                      "cudaMemcpyAsync(logits)");
+        if (next_token)
+            CheckCuda(cudaMemcpyAsync(h + 3, session->state + 2, sizeof(int), cudaMemcpyDeviceToHost,
+                                      c.stream),
+                      "cudaMemcpyAsync(next)");
+        CheckStatus(session, c);
+        if (next_token) *next_token = h[3];
+    });
+}
+
+int mlb_session_generate(mlb_session* session, const int* prompt, int n_prompt, int start_pos,
+                         int n_new, int* out_tokens) {
+    return Guard([&] {
+        const char* w = "mlb_session_generate";
+        Require(session && prompt && out_tokens, w, "null argument");
+        Require(n_prompt > 0 && n_new > 0, w, "prompt and generation must be non-empty");
+        const mlb_model_config& cf = session->model->cfg;
+        Require(start_pos >= 0 && start_pos + n_prompt + n_new - 1 <= cf.max_seq_len, w,
+                "position out of range", MLB_ERR_OUT_OF_RANGE);
+        for (int i = 0; i < n_prompt; ++i)
+            Require(prompt[i] >= 0 && prompt[i] < cf.vocab_size, w, "token id out of range",
+                    MLB_ERR_OUT_OF_RANGE);
+        DeviceContext& c = Ctx(session->model->device);
+        CheckCuda(cudaMemcpyAsync(session->hist + start_pos, prompt, size_t(n_prompt) * 4,
+                                  cudaMemcpyHostToDevice, c.stream),
+                  "cudaMemcpyAsync(prompt)");
+        SetState(session, c, start_pos, start_pos + n_prompt);
+        const int steps = n_prompt + n_new - 1;
+        for (int i = 0; i < steps; ++i)
+            CheckCuda(cudaGraphLaunch(session->exec, c.stream), "cudaGraphLaunch");
+        CheckCuda(cudaMemcpyAsync(out_tokens, session->hist + start_pos + n_prompt, size_t(n_new) * 4,
+                                  cudaMemcpyDeviceToHost, c.stream),
+                  "cudaMemcpyAsync(tokens)");
+        CheckStatus(session, c);
+    });
+}
+
+int mlb_session_decode_device(mlb_session* session, int* tokens, int start_pos, int n_steps) {
+    return Guard([&] {
+        const char* w = "mlb_session_decode_device";
+        Require(session && tokens, w, "null argument");
+        Require(n_steps > 0, w, "n_steps must be positive");
+        const mlb_model_config& cf = session->model->cfg;
+        Require(start_pos >= 0 && start_pos + n_steps <= cf.max_seq_len, w,
+                "position out of range", MLB_ERR_OUT_OF_RANGE);
+        DeviceContext& c = Ctx(session->model->device);
+        CheckCuda(cudaMemcpyAsync(session->hist + start_pos, tokens, sizeof(int),
+                                  cudaMemcpyDeviceToDevice, c.stream),
+                  "cudaMemcpyAsync(token)");
+        SetState(session, c, start_pos, start_pos + 1);
+        for (int i = 0; i < n_steps; ++i)
+            CheckCuda(cudaGraphLaunch(session->exec, c.stream), "cudaGraphLaunch");
+        CheckCuda(cudaMemcpyAsync(tokens + 1, session->hist + start_pos + 1, size_t(n_steps) * 4,
+                                  cudaMemcpyDeviceToDevice, c.stream),
+                  "cudaMemcpyAsync(tokens)");
+    });
+}
+
+int mlb_session_logits(mlb_session* session, const float** logits) {
+    return Guard([&] {
+        Require(session && logits, "mlb_session_logits", "null argument");
+        *logits = session->logits;
+    });
+}
+
+int mlb_session_kv_cache(mlb_session* session, float** key_cache, float** value_cache) {
+    return Guard([&] {
+        Require(session && key_cache && value_cache, "mlb_session_kv_cache", "null argument");
+        *key_cache = session->kc;
+        *value_cache = session->vc;
+    });
+}
+
+}  // extern "C"

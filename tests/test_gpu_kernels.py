@@ -1,0 +1,314 @@
+"""GPU parity of the op-level C ABI against the oracle and the reference's own
+golden vectors.
+
+Tolerances (mixed absolute/relative as in the reference's RequireClose,
+test/gpu_core_test.cpp:35-53: |a - e| <= tol * max(1, |e|)):
+  - quantized linear: 1e-4 (the target for quantized linear outputs)
+  - attention, RMSNorm, SiLU, softmax: 1e-4
+  - RoPE, quantization, dequantization, KV write, embedding, arg-max and the
+    synthetic generator: bit-exact
+"""
+import ctypes
+
+import numpy as np
+import pytest
+
+from mini_llama_b200 import capi
+from mini_llama_b200.device import DeviceArray
+from oracle.binding import BLOCK_BYTES, Q40, Q41, Q80, STREAM_W, STREAM_X
+
+pytestmark = pytest.mark.gpu
+
+LIN_TOL = 1e-4
+OP_TOL = 1e-4
+QNAME = {Q80: "q8_0", Q40: "q4_0", Q41: "q4_1"}
+LINEAR_SHAPES = [(5, 13), (5, 32), (5, 33), (5, 64), (5, 129), (7, 176), (16, 896), (3, 4864)]
+
+
+def assert_close(actual, expected, tol, what):
+    a = np.asarray(actual, np.float64).ravel()
+    e = np.asarray(expected, np.float64).ravel()
+    assert a.shape == e.shape, what
+    assert np.all(np.isfinite(a)), f"{what}: non-finite output"
+    err = np.abs(a - e)
+    bound = tol * np.maximum(1.0, np.abs(e))
+    bad = np.flatnonzero(err > bound)
+    assert bad.size == 0, (f"{what}: {bad.size} of {a.size} outside {tol}, worst "
+                           f"{float((err / np.maximum(1.0, np.abs(e))).max()):.3e} at {bad[:4]}")
+
+
+def linear_gpu(mlb, dev, qtype, x, blocks, n, bias=None):
+    x = np.ascontiguousarray(x, np.float32)
+    rows, k = (1, x.shape[0]) if x.ndim == 1 else x.shape
+    xd = DeviceArray.from_host(mlb, dev, x)
+    wd = DeviceArray.from_host(mlb, dev, blocks)
+    bd = DeviceArray.from_host(mlb, dev, bias) if bias is not None else None
+    yd = DeviceArray(mlb, dev, (rows, n))
+    nb = (k + 31) // 32
+    mlb.call("mlb_quant_linear", dev, qtype, xd.ptr, wd.ptr, n * nb, rows, k, n,
+             bd.ptr if bd else None, yd.ptr)
+    return yd.download().reshape((n,) if x.ndim == 1 else (rows, n))
+
+
+@pytest.mark.parametrize("qtype", [Q80, Q40, Q41])
+@pytest.mark.parametrize("idx,shape", list(enumerate(LINEAR_SHAPES)))
+def test_linear_matches_reference_golden(mlb, gpu, oracle, golden_ops, qtype, idx, shape):
+    n, k = shape
+    tag = f"{n}x{k}"
+    name = {Q80: "80", Q40: "40", Q41: "41"}[qtype]
+    blocks = golden_ops[f"q{name}_{tag}"]
+    x = oracle.normal(3 * k, 2, STREAM_X + 16 * idx, 1.0).reshape(3, k)
+    x1 = oracle.normal(k, 2, STREAM_X + 16 * idx + 1, 1.0)
+    assert_close(linear_gpu(mlb, gpu, qtype, x, blocks, n), golden_ops[f"lin{name}_{tag}"],
+                 LIN_TOL, f"{QNAME[qtype]} batch {tag}")
+    assert_close(linear_gpu(mlb, gpu, qtype, x1, blocks, n), golden_ops[f"lin{name}v_{tag}"],
+                 LIN_TOL, f"{QNAME[qtype]} 1-D {tag}")
+    bias = oracle.normal(n, 2, 999, 0.1)
+    assert_close(linear_gpu(mlb, gpu, qtype, x1, blocks, n, bias),
+                 golden_ops[f"lin{name}v_{tag}"] + bias, LIN_TOL, f"{QNAME[qtype]} bias {tag}")
+
+
+BENCH_SHAPES = [(896, 896), (4864, 896), (896, 4864), (151936, 896)]
+_WEIGHTS = {}
+
+
+def bench_blocks(oracle, qtype, n, k):
+    key = (qtype, n, k)
+    if key not in _WEIGHTS:
+        w = oracle.normal(n * k, 2, STREAM_W + 1000 + n + k, 0.02).reshape(n, k)
+        _WEIGHTS[key] = oracle.quantize(qtype, w)
+    return _WEIGHTS[key]
+
+
+@pytest.mark.parametrize("qtype", [Q80, Q40, Q41])
+@pytest.mark.parametrize("n,k", BENCH_SHAPES)
+@pytest.mark.parametrize("m", [1, 8])
+def test_linear_microbench_shapes(mlb, gpu, oracle, qtype, n, k, m):
+    blocks = bench_blocks(oracle, qtype, n, k)
+    x = oracle.normal(m * k, 2, STREAM_X + 1000 + n + k, 1.0).reshape(m, k)
+    expect = oracle.linear(qtype, x, blocks, n)
+    assert_close(linear_gpu(mlb, gpu, qtype, x, blocks, n), expect, LIN_TOL,
+                 f"{QNAME[qtype]} [{n},{k}] M={m}")
+
+
+def test_linear_misaligned_weight_pointer(mlb, gpu, oracle):
+    """A weight pointer off the 16-byte grid takes the direct-load kernel."""
+    n, k = 33, 96
+    w = oracle.normal(n * k, 2, 77, 0.02).reshape(n, k)
+    blocks = oracle.quantize(Q80, w)
+    x = oracle.normal(2 * k, 2, 78, 1.0).reshape(2, k)
+    buf = DeviceArray(mlb, gpu, blocks.nbytes + 16, np.uint8)
+    shifted = np.zeros(blocks.nbytes + 16, np.uint8)
+    shifted[2:2 + blocks.nbytes] = blocks
+    buf.upload(shifted)
+    xd = DeviceArray.from_host(mlb, gpu, x)
+    yd = DeviceArray(mlb, gpu, (2, n))
+    mlb.call("mlb_q80_linear", gpu, xd.ptr, buf.ptr + 2, blocks.nbytes // 34, 2, k, n, None,
+             yd.ptr)
+    assert_close(yd.download(), oracle.linear(Q80, x, blocks, n), LIN_TOL, "misaligned")
+
+
+def test_linear_rejects_bad_block_count(mlb, gpu):
+    xd = DeviceArray(mlb, gpu, 32)
+    wd = DeviceArray(mlb, gpu, 34 * 4, np.uint8)
+    yd = DeviceArray(mlb, gpu, 4)
+    st = mlb.raw("mlb_q80_linear", gpu, xd.ptr, wd.ptr, 3, 1, 32, 4, None, yd.ptr)
+    assert st == capi.MLB_ERR_INVALID_ARGUMENT
+    assert "block count mismatch: expected 4, got 3" in mlb.last_error()
+    assert mlb.raw("mlb_q80_linear", gpu, xd.ptr, None, 4, 1, 32, 4, None, yd.ptr) != 0
+    assert "null" in mlb.last_error()
+
+
+@pytest.mark.parametrize("qtype", [Q80, Q40, Q41])
+def test_device_quantizer_bit_exact(mlb, gpu, oracle, golden_ops, qtype):
+    name = {Q80: "80", Q40: "40", Q41: "41"}[qtype]
+    for idx, (n, k) in enumerate(LINEAR_SHAPES):
+        w = oracle.normal(n * k, 2, STREAM_W + 16 * idx, 0.02).reshape(n, k)
+        wd = DeviceArray.from_host(mlb, gpu, w)
+        nb = (k + 31) // 32
+        qd = DeviceArray(mlb, gpu, n * nb * BLOCK_BYTES[qtype], np.uint8)
+        mlb.call("mlb_quantize", gpu, qtype, wd.ptr, n, k, qd.ptr)
+        got = qd.download()
+        assert np.array_equal(got, golden_ops[f"q{name}_{n}x{k}"]), f"quantize {qtype} {n}x{k}"
+        yd = DeviceArray(mlb, gpu, (n, k))
+        mlb.call("mlb_dequantize", gpu, qtype, qd.ptr, n, k, yd.ptr)
+        ref = golden_ops[f"deq{name}_{n}x{k}"]
+        assert np.array_equal(yd.download().view(np.uint32).ravel(), ref.view(np.uint32)), \
+            f"dequantize {qtype} {n}x{k}"
+
+
+def test_device_quantizer_fp16_probes(mlb, gpu, golden_ops):
+    probes = golden_ops["fp16_probes"]
+    blocks = np.zeros((len(probes), 32), np.float32)
+    blocks[:, 0] = probes
+    blocks[:, 7] = probes * np.float32(0.25)
+    xd = DeviceArray.from_host(mlb, gpu, blocks)
+    for qtype, key, bb in ((Q80, "fp16_q80_d", 34), (Q40, "fp16_q40_d", 18)):
+        qd = DeviceArray(mlb, gpu, len(probes) * bb, np.uint8)
+        mlb.call("mlb_quantize", gpu, qtype, xd.ptr, len(probes), 32, qd.ptr)
+        d = qd.download().reshape(len(probes), bb)[:, :2].copy().view(np.uint16).ravel()
+        assert np.array_equal(d, golden_ops[key]), key
+
+
+def test_synth_device_matches_host(mlb, gpu, oracle):
+    for seed, stream, sigma, n in ((3, 1, 0.02, 100003), (4, 1005, 1.0, 4096), (2, 8, 0.02, 17)):
+        d = DeviceArray(mlb, gpu, n)
+        mlb.call("mlb_synth_normal", gpu, d.ptr, n, seed, stream, sigma)
+        host = oracle.normal(n, seed, stream, sigma)
+        assert np.array_equal(d.download().view(np.uint32), host.view(np.uint32))
+
+
+def test_rmsnorm(mlb, gpu, oracle, golden_ops):
+    for idx, n in enumerate((129, 896, 4096)):
+        x = oracle.normal(n, 2, 100 + idx, 1.0)
+        w = (np.float32(1.0) + oracle.normal(n, 2, 200 + idx, 0.1)).astype(np.float32)
+        xd, wd, yd = (DeviceArray.from_host(mlb, gpu, x), DeviceArray.from_host(mlb, gpu, w),
+                      DeviceArray(mlb, gpu, n))
+        for eps, tag in ((1e-5, "e5"), (1e-6, "e6")):
+            mlb.call("mlb_rmsnorm", gpu, xd.ptr, wd.ptr, n, eps, yd.ptr)
+            assert_close(yd.download(), golden_ops[f"rmsnorm_{n}_{tag}"], OP_TOL, f"rmsnorm {n}")
+
+
+def test_activations_softmax_argmax(mlb, gpu, oracle, golden_ops):
+    g = oracle.normal(4864, 2, 300, 2.0)
+    u = oracle.normal(4864, 2, 301, 1.0)
+    gd, ud, yd = (DeviceArray.from_host(mlb, gpu, g), DeviceArray.from_host(mlb, gpu, u),
+                  DeviceArray(mlb, gpu, 4864))
+    mlb.call("mlb_silu", gpu, gd.ptr, 4864, yd.ptr)
+    assert_close(yd.download(), golden_ops["silu"], OP_TOL, "silu")
+    mlb.call("mlb_mul", gpu, gd.ptr, ud.ptr, 4864, yd.ptr)
+    assert np.array_equal(yd.download(), g * u)
+    mlb.call("mlb_add", gpu, gd.ptr, ud.ptr, 4864, yd.ptr)
+    assert np.array_equal(yd.download(), g + u)
+    mlb.call("mlb_softmax", gpu, gd.ptr, 4864, yd.ptr)
+    assert_close(yd.download(), golden_ops["softmax"], OP_TOL, "softmax")
+    out = DeviceArray(mlb, gpu, 1, np.int32)
+    ties = np.array([0.5, 2.0, -1.0, 2.0, 1.0, 2.0, 0.0, -3.0, 1.5], np.float32)
+    got = []
+    for v in (ties, g, u):
+        vd = DeviceArray.from_host(mlb, gpu, v)
+        mlb.call("mlb_argmax", gpu, vd.ptr, len(v), out.ptr)
+        got.append(int(out.download()[0]))
+    assert got == list(golden_ops["argmax"])
+
+
+ROPE_CASES = [
+    ("qwen2", 64, 14, 2, 1e6, 1, [0, 1, 63, 191, 8191, 32767]),
+    ("llama", 128, 32, 8, 1e4, 0, [0, 5, 511, 767]),
+    ("tiny", 16, 4, 2, 1e4, 0, [0, 3, 11, 127]),
+    ("gputest_normal", 14, 4, 2, 1e4, 0, [3, 11]),
+    ("gputest_neox", 14, 4, 2, 1e4, 1, [3, 11]),
+]
+
+
+def test_rope_bit_exact(mlb, gpu, oracle, golden_ops):
+    idx = 0
+    for tag, hd, nh, nkv, theta, neox, positions in ROPE_CASES:
+        for pos in positions:
+            q = oracle.normal(nh * hd, 4, 400 + idx, 1.0)
+            k = oracle.normal(nkv * hd, 4, 500 + idx, 1.0)
+            qd, kd = DeviceArray.from_host(mlb, gpu, q), DeviceArray.from_host(mlb, gpu, k)
+            mlb.call("mlb_rope", gpu, qd.ptr, kd.ptr, nh, nkv, hd, pos, theta,
+                     capi.ROPE_NEOX if neox else capi.ROPE_NORMAL)
+            for got, key in ((qd.download(), f"rope_q_{tag}_p{pos}"),
+                             (kd.download(), f"rope_k_{tag}_p{pos}")):
+                assert np.array_equal(got.view(np.uint32), golden_ops[key].view(np.uint32)), key
+            idx += 1
+
+
+def test_embedding_and_kv_write(mlb, gpu, oracle):
+    table = oracle.normal(50 * 24, 9, 1, 1.0).reshape(50, 24)
+    td, yd = DeviceArray.from_host(mlb, gpu, table), DeviceArray(mlb, gpu, 24)
+    mlb.call("mlb_embedding", gpu, td.ptr, 50, 24, 37, yd.ptr)
+    assert np.array_equal(yd.download(), table[37])
+    assert mlb.raw("mlb_embedding", gpu, td.ptr, 50, 24, 50, yd.ptr) == capi.MLB_ERR_INVALID_ARGUMENT
+    layers, seq, nkv, hd = 3, 9, 2, 8
+    kc = DeviceArray(mlb, gpu, (layers, seq, nkv, hd))
+    vc = DeviceArray(mlb, gpu, (layers, seq, nkv, hd))
+    mlb.call("mlb_memset", gpu, kc.ptr, 0, kc.nbytes)
+    mlb.call("mlb_memset", gpu, vc.ptr, 0, vc.nbytes)
+    k = oracle.normal(nkv * hd, 9, 2, 1.0)
+    v = oracle.normal(nkv * hd, 9, 3, 1.0)
+    kd, vd = DeviceArray.from_host(mlb, gpu, k), DeviceArray.from_host(mlb, gpu, v)
+    mlb.call("mlb_kv_write", gpu, kc.ptr, vc.ptr, layers, seq, nkv, hd, 2, 5, kd.ptr, vd.ptr)
+    K, V = kc.download(), vc.download()
+    assert np.array_equal(K[2, 5].ravel(), k) and np.array_equal(V[2, 5].ravel(), v)
+    K[2, 5] = 0
+    V[2, 5] = 0
+    assert not K.any() and not V.any()
+    st = mlb.raw("mlb_kv_write", gpu, kc.ptr, vc.ptr, layers, seq, nkv, hd, 2, seq, kd.ptr, vd.ptr)
+    assert st == capi.MLB_ERR_OUT_OF_RANGE and "position out of range" in mlb.last_error()
+
+
+def attention_inputs(oracle, layers, layer, pos, nh, nkv, hd, stream, max_seq=None):
+    max_seq = max_seq or pos + 1
+    per_layer = (pos + 1) * nkv * hd
+    kc = np.zeros((layers, max_seq, nkv, hd), np.float32)
+    vc = np.zeros_like(kc)
+    kc[layer, :pos + 1] = oracle.normal(per_layer, 4, stream + 1, 1.0).reshape(pos + 1, nkv, hd)
+    vc[layer, :pos + 1] = oracle.normal(per_layer, 4, stream + 2, 1.0).reshape(pos + 1, nkv, hd)
+    q = oracle.normal(nh * hd, 4, stream, 1.0).reshape(nh, hd)
+    return q, kc, vc
+
+
+def attention_gpu(mlb, dev, q, kc, vc, layer, pos, nh, nkv, hd):
+    qd, kd, vd = (DeviceArray.from_host(mlb, dev, q), DeviceArray.from_host(mlb, dev, kc),
+                  DeviceArray.from_host(mlb, dev, vc))
+    od = DeviceArray(mlb, dev, (nh, hd))
+    mlb.call("mlb_attention_decode", dev, qd.ptr, kd.ptr, vd.ptr, kc.shape[0], kc.shape[1],
+             layer, pos, nh, nkv, hd, od.ptr)
+    return od.download()
+
+
+def test_attention_reference_grid(mlb, gpu, oracle, golden_ops):
+    stream = 1000
+    for hd in (7, 128, 129):
+        for pos in (0, 4, 126, 127, 128, 256):
+            q, kc, vc = attention_inputs(oracle, 2, 1, pos, 4, 2, hd, stream)
+            got = attention_gpu(mlb, gpu, q, kc, vc, 1, pos, 4, 2, hd)
+            assert_close(got, golden_ops[f"attn_grid_hd{hd}_p{pos}"], OP_TOL,
+                         f"attention hd={hd} pos={pos}")
+            stream += 8
+
+
+@pytest.mark.parametrize("shape", [(14, 2, 64), (32, 8, 128)])
+def test_attention_sweep(mlb, gpu, oracle, golden_ops, shape):
+    nh, nkv, hd = shape
+    stream = 1000 + 18 * 8 + (0 if nh == 14 else 4 * 8)
+    for pos in (127, 1023, 8191, 32767):
+        q, kc, vc = attention_inputs(oracle, 1, 0, pos, nh, nkv, hd, stream)
+        got = attention_gpu(mlb, gpu, q, kc, vc, 0, pos, nh, nkv, hd)
+        assert_close(got, golden_ops[f"attn_sweep_{nh}x{hd}_p{pos}"], OP_TOL,
+                     f"sweep {nh}x{hd} pos={pos}")
+        stream += 8
+
+
+def test_attention_batched_independent_sequences(mlb, gpu, oracle):
+    """32 sequences with different lengths in one call equal 32 single calls."""
+    batch, nh, nkv, hd, max_seq, layers = 32, 14, 2, 64, 300, 2
+    rng = np.random.default_rng(4)
+    positions = rng.integers(0, max_seq, batch).astype(np.int32)
+    positions[0], positions[1] = 0, max_seq - 1
+    kc = oracle.normal(batch * layers * max_seq * nkv * hd, 4, 7000, 1.0).reshape(
+        batch, layers, max_seq, nkv, hd)
+    vc = oracle.normal(batch * layers * max_seq * nkv * hd, 4, 7001, 1.0).reshape(kc.shape)
+    q = oracle.normal(batch * nh * hd, 4, 7002, 1.0).reshape(batch, nh, hd)
+    qd, kd, vd = (DeviceArray.from_host(mlb, gpu, q), DeviceArray.from_host(mlb, gpu, kc),
+                  DeviceArray.from_host(mlb, gpu, vc))
+    pd = DeviceArray.from_host(mlb, gpu, positions)
+    od = DeviceArray(mlb, gpu, (batch, nh, hd))
+    mlb.call("mlb_attention_decode_batched", gpu, batch, qd.ptr, kd.ptr, vd.ptr, layers, max_seq,
+             1, pd.ptr, int(positions.max()), nh, nkv, hd, od.ptr)
+    got = od.download()
+    for b in range(batch):
+        ref = oracle.attention(q[b], kc[b], vc[b], 1, int(positions[b]), nh, nkv, hd)
+        assert_close(got[b], ref, OP_TOL, f"sequence {b} pos={positions[b]}")
+
+
+def test_attention_validation(mlb, gpu):
+    q = DeviceArray(mlb, gpu, 64)
+    kc = DeviceArray(mlb, gpu, 2 * 4 * 64)
+    st = mlb.raw("mlb_attention_decode", gpu, q.ptr, kc.ptr, kc.ptr, 1, 4, 0, 4, 1, 1, 64, q.ptr)
+    assert st == capi.MLB_ERR_OUT_OF_RANGE
+    st = mlb.raw("mlb_attention_decode", gpu, q.ptr, kc.ptr, kc.ptr, 1, 4, 0, 1, 3, 2, 64, q.ptr)
+    assert st == capi.MLB_ERR_INVALID_ARGUMENT and "divisible" in mlb.last_error()
