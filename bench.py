@@ -32,7 +32,7 @@ sys.path.insert(0, ROOT)
 METRIC = "decode tok/s (Qwen2-0.5B-arch Q8_0, bs1)"
 UNIT = "tokens/s"
 PROMPT = 64
-NEW = 128
+NEW = 128  # decode tokens per step (bench --decode-tokens may lower it for profiling)
 QWEN2 = dict(vocab_size=151936, dim=896, hidden_dim=4864, n_layers=24, n_heads=14, n_kv_heads=2,
              head_dim=64, max_seq_len=256, rope_theta=1e6, rms_norm_eps=1e-6, rope_neox=1,
              qkv_bias=1, tied_embedding=1, qtype=1, seed=3, prompt_seed=3)
@@ -200,20 +200,30 @@ def run_ours(args):
     lib = capi.load()
     dev = local
     stream = torch.cuda.ExternalStream(lib.stream(dev), device=torch.device("cuda", dev))
+    if args.roofline_only:
+        algo, launch_s = gemv_roofline(lib, dev, torch, stream)
+        print(json.dumps({"kernel": "GemvKernel<Q8_0, M=1> on [151936, 896]", "bytes": algo,
+                          "launch_us": launch_s * 1e6, "gbs": algo / launch_s / 1e9}))
+        return 0
 
     model = Model(lib, dev, QWEN2)
     model.synthesize(seed=QWEN2["seed"], tied=True)
     sess = Session(model)
     from oracle.binding import Oracle  # only for the prompt ids (seeded generator)
     prompt = Oracle().tokens(PROMPT, QWEN2["prompt_seed"], QWEN2["vocab_size"])
-    first = sess.generate(prompt, 1)  # prefill, first greedy token at position 64
+    if args.no_prefill:  # profiling runs: decode from position 64 over an empty cache
+        first = np.array([int(prompt[-1])], np.int32)
+    else:
+        first = sess.generate(prompt, 1)  # prefill, first greedy token at position 64
     toks = DeviceArray(lib, dev, NEW + 1, np.int32)
     init = np.zeros(NEW + 1, np.int32)
     init[0] = first[0]
     toks.upload(init)
 
+    new = args.decode_tokens
+
     def step():
-        sess.decode_device(toks.ptr, PROMPT, NEW)
+        sess.decode_device(toks.ptr, PROMPT, new)
 
     def barrier():
         torch.cuda.synchronize(dev)
@@ -239,7 +249,7 @@ def run_ours(args):
         t = torch.tensor([secs], device=f"cuda:{dev}")
         dist.all_reduce(t, op=dist.ReduceOp.MAX)
         secs = float(t.item())
-    value = world * NEW * args.steps / secs
+    value = world * new * args.steps / secs
 
     # e2e: host start token in, host token ids out, through mlb_session_generate
     start = torch.empty(1, dtype=torch.int32, pin_memory=True)
@@ -250,25 +260,27 @@ def run_ours(args):
         lib.call("mlb_session_generate", sess.handle, start.data_ptr(), 1, PROMPT, NEW,
                  out.data_ptr())
 
-    for _ in range(max(1, args.warmup)):
-        e2e_step()
-    barrier()
-    t0 = time.perf_counter()
-    for _ in range(args.steps):
-        e2e_step()
-    barrier()
-    e2e_secs = time.perf_counter() - t0
-    if dist is not None:
-        t = torch.tensor([e2e_secs], device=f"cuda:{dev}")
-        dist.all_reduce(t, op=dist.ReduceOp.MAX)
-        e2e_secs = float(t.item())
-    e2e = world * NEW * args.steps / e2e_secs
+    e2e = None
+    if not args.no_e2e:
+        for _ in range(max(1, args.warmup)):
+            e2e_step()
+        barrier()
+        t0 = time.perf_counter()
+        for _ in range(args.steps):
+            e2e_step()
+        barrier()
+        e2e_secs = time.perf_counter() - t0
+        if dist is not None:
+            t = torch.tensor([e2e_secs], device=f"cuda:{dev}")
+            dist.all_reduce(t, op=dist.ReduceOp.MAX)
+            e2e_secs = float(t.item())
+        e2e = world * NEW * args.steps / e2e_secs
 
     peaks = measured_peaks()
     algo, launch_s = gemv_roofline(lib, dev, torch, stream)
     achieved = algo / launch_s / 1e9
-    step_bytes = sum(algorithmic_bytes_per_token(p) for p in range(PROMPT, PROMPT + NEW))
-    step_gbs = step_bytes * args.steps / (secs / world * world) / 1e9 if world == 1 else None
+    step_bytes = sum(algorithmic_bytes_per_token(p) for p in range(PROMPT, PROMPT + new))
+    step_gbs = step_bytes * args.steps / secs / 1e9 if world == 1 else None
     launches_per_token = 1 + 5 * QWEN2["n_layers"] + 1
 
     sess.close()
@@ -295,18 +307,19 @@ def run_ours(args):
         "data": "synthetic (seeded random-init weights and prompt ids)",
         "config": dict(CONFIG, parallelism=f"replicas x{world}" if world > 1 else "single GPU"),
         "e2e": {"value": e2e, "unit": UNIT, "h2d_bytes_per_step": 4 + 8 + 4,
-                "d2h_bytes_per_step": NEW * 4 + 4},
+                "d2h_bytes_per_step": NEW * 4 + 4,
+                "path": "mlb_session_generate(host start token -> host 128 token ids)"},
         "roofline": {"bound": "hbm", "kernel": "GemvKernel<Q8_0, M=1> on [151936, 896]",
                      "achieved": achieved, "peak": peaks["hbm_gbs"], "unit": "GB/s",
                      "frac": achieved / peaks["hbm_gbs"], "peak_source": peaks["source"],
                      "bytes_per_launch": algo, "launch_us": launch_s * 1e6,
                      "traffic": committed_traffic("gemv_q80_lm_head")},
-        "step_roofline": {"bytes_per_token_avg": step_bytes / NEW,
+        "step_roofline": {"bytes_per_token_avg": step_bytes / new,
                           "achieved_gbs": step_gbs,
                           "frac": (step_gbs / peaks["hbm_gbs"]) if step_gbs else None},
         "cpu_baseline": cpu,
         "clocks": clk,
-        "gpu_launches": launches_per_token * NEW * args.steps,
+        "gpu_launches": launches_per_token * new * args.steps,
     }
     print(json.dumps(line), flush=True)
     return 0
@@ -319,6 +332,13 @@ def main():
     ap.add_argument("--warmup", type=int, default=3)
     ap.add_argument("--impl", default="ours", choices=["ours", "reference"])
     ap.add_argument("--no-cpu-baseline", action="store_true")
+    ap.add_argument("--no-e2e", action="store_true")
+    ap.add_argument("--no-prefill", action="store_true",
+                    help="profiling: skip the 64-token prefill (KV cache left empty)")
+    ap.add_argument("--roofline-only", action="store_true",
+                    help="time only the Q8_0 GEMV on the lm_head shape")
+    ap.add_argument("--decode-tokens", type=int, default=NEW,
+                    help="tokens per step (128 for the headline; fewer for profiling runs)")
     args = ap.parse_args()
     if args.impl == "reference":
         return run_reference(args)

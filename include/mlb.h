@@ -99,6 +99,20 @@ int mlb_q41_linear(int device, const float* x, const void* w, size_t block_count
 int mlb_quant_linear(int device, int qtype, const float* x, const void* w, size_t block_count,
                      int rows, int in_features, int out_features, const float* bias, float* y);
 
+/* Prepared Q8_0 weights ("R16" layout): the same bytes regrouped into 16-row
+ * tiles of 544-byte chunks (16 x 32 int8 quants, then 16 fp16 scales), every
+ * chunk 16-byte aligned.  A caller that keeps a prepared copy gets the
+ * tensor-core GEMV, which computes each block's dot product exactly in int32
+ * (x split into three int8 digit planes per 32-element block) and applies the
+ * scales in fp32.  No reference counterpart: the reference reads the GGUF
+ * blocks in place; this is the layout its weights take inside the decode
+ * session.  mlb_r16_bytes returns the size of the prepared copy (rows padded
+ * to a multiple of 16). */
+size_t mlb_r16_bytes(int rows, int cols);
+int mlb_q80_repack_r16(int device, const void* w, int rows, int cols, void* w_r16);
+int mlb_q80_linear_r16(int device, const float* x, const void* w_r16, int rows, int in_features,
+                       int out_features, const float* bias, float* y);
+
 /* ------------------------------------------------------------ quantization
  * Device quantizer, bit-identical to the reference's QuantizeToQ80 and
  * QuantizeToQ40 (src/quant.cpp:104-240, fp16 rounding of src/quant.cpp:17-52)

@@ -58,10 +58,14 @@ struct AttnParams {
     int neox;
 };
 
+// K and V tiles are fetched together (two buffers per warp) for head_dim <=
+// 128; above that one buffer is reused (K, then V) to fit shared memory.
+__host__ __device__ inline int AttnTileBuffers(int hd) { return hd <= 128 ? 2 : 1; }
+
 __host__ __device__ inline size_t AttnSmemBytes(int hd) {
     const size_t row = size_t(hd) + 1;
     return (size_t(kAttnGmax) * hd +                      // q
-            size_t(kAttnWarps) * kAttnTile * row +        // K/V tile per warp
+            size_t(AttnTileBuffers(hd)) * kAttnWarps * kAttnTile * row +  // K/V tiles
             size_t(kAttnWarps) * kAttnGmax * kAttnTile +  // probabilities per warp
             size_t(kAttnWarps) * kAttnGmax * 2 +          // (m, l) per warp
             size_t(kAttnWarps) * kAttnGmax * hd) * 4;     // o per warp
@@ -72,9 +76,10 @@ __global__ void __launch_bounds__(kAttnThreads) AttnSplitKernel(const AttnParams
     extern __shared__ __align__(16) float asmem[];
     const int hd = p.hd;
     const int row = hd + 1;
+    const int nbuf = AttnTileBuffers(hd);
     float* qs = asmem;                                         // [G][hd]
-    float* tiles = qs + kAttnGmax * hd;                        // [W][32][row]
-    float* probs = tiles + kAttnWarps * kAttnTile * row;       // [W][G][32]
+    float* tiles = qs + kAttnGmax * hd;                        // [nbuf][W][32][row]
+    float* probs = tiles + nbuf * kAttnWarps * kAttnTile * row;  // [W][G][32]
     float* mls = probs + kAttnWarps * kAttnGmax * kAttnTile;   // [W][G][2]
     float* os = mls + kAttnWarps * kAttnGmax * 2;              // [W][G][hd]
 
@@ -146,15 +151,23 @@ __global__ void __launch_bounds__(kAttnThreads) AttnSplitKernel(const AttnParams
         for (int j = 0; j < DPL; ++j) o[g][j] = 0.0f;
     }
     float* tile = tiles + warp * kAttnTile * row;
+    float* vtile = nbuf == 2 ? tiles + (kAttnWarps + warp) * kAttnTile * row : tile;
     float* pr = probs + warp * kAttnGmax * kAttnTile;
 
     for (int t0 = p0 + warp * kAttnTile; t0 < p1; t0 += kAttnWarps * kAttnTile) {
         const int tn = min(kAttnTile, p1 - t0);
-        // K tile -> shared (coalesced along hd)
+        // K (and V) tile -> shared with asynchronous copies, all in flight
         for (int r = 0; r < tn; ++r) {
             const float* src = kbase + size_t(t0 + r) * pos_stride;
-            for (int d = lane; d < hd; d += 32) tile[r * row + d] = src[d];
+            for (int d = lane; d < hd; d += 32) CpAsync4(tile + r * row + d, src + d);
         }
+        if (nbuf == 2) {
+            for (int r = 0; r < tn; ++r) {
+                const float* src = vbase + size_t(t0 + r) * pos_stride;
+                for (int d = lane; d < hd; d += 32) CpAsync4(vtile + r * row + d, src + d);
+            }
+        }
+        CpAsyncWaitAll();
         __syncwarp();
         float s[kAttnGmax];
 #pragma unroll
@@ -183,18 +196,20 @@ __global__ void __launch_bounds__(kAttnThreads) AttnSplitKernel(const AttnParams
             pr[g * kAttnTile + lane] = pv;
         }
         __syncwarp();
-        // V tile replaces K
-        for (int r = 0; r < tn; ++r) {
-            const float* src = vbase + size_t(t0 + r) * pos_stride;
-            for (int d = lane; d < hd; d += 32) tile[r * row + d] = src[d];
+        if (nbuf == 1) {  // V tile replaces K
+            for (int r = 0; r < tn; ++r) {
+                const float* src = vbase + size_t(t0 + r) * pos_stride;
+                for (int d = lane; d < hd; d += 32) CpAsync4(vtile + r * row + d, src + d);
+            }
+            CpAsyncWaitAll();
+            __syncwarp();
         }
-        __syncwarp();
         for (int r = 0; r < tn; ++r) {
 #pragma unroll
             for (int j = 0; j < DPL; ++j) {
                 const int d = lane + 32 * j;
                 if (d < hd) {
-                    float vv = tile[r * row + d];
+                    float vv = vtile[r * row + d];
 #pragma unroll
                     for (int g = 0; g < kAttnGmax; ++g)
                         if (g < gcnt) o[g][j] = fmaf(pr[g * kAttnTile + r], vv, o[g][j]);

@@ -169,6 +169,34 @@ __device__ __forceinline__ void BulkLoad(void* smem_dst, const void* gmem_src, u
         : "memory");
 }
 
+// Asynchronous global -> shared copies (cp.async): every copy of a batch is in
+// flight at once, so staging a vector costs one memory round trip.
+__device__ __forceinline__ void CpAsync4(void* smem_dst, const void* gmem_src) {
+    asm volatile("cp.async.ca.shared.global [%0], [%1], 4;" ::"r"(SmemAddr(smem_dst)),
+                 "l"(gmem_src)
+                 : "memory");
+}
+__device__ __forceinline__ void CpAsync16(void* smem_dst, const void* gmem_src) {
+    asm volatile("cp.async.cg.shared.global [%0], [%1], 16;" ::"r"(SmemAddr(smem_dst)),
+                 "l"(gmem_src)
+                 : "memory");
+}
+__device__ __forceinline__ void CpAsyncWaitAll() {
+    asm volatile("cp.async.commit_group;\ncp.async.wait_group 0;" ::: "memory");
+}
+
+// Block-cooperative staging of n floats into shared memory (no wait).
+__device__ __forceinline__ void StageFloats(float* dst, const float* src, int n) {
+    const bool vec = ((reinterpret_cast<uintptr_t>(src) | reinterpret_cast<uintptr_t>(dst)) & 15) == 0;
+    int done = 0;
+    if (vec) {
+        const int n4 = n >> 2;
+        for (int i = threadIdx.x; i < n4; i += blockDim.x) CpAsync16(dst + 4 * i, src + 4 * i);
+        done = n4 << 2;
+    }
+    for (int i = done + threadIdx.x; i < n; i += blockDim.x) CpAsync4(dst + i, src + i);
+}
+
 // L2 prefetch of a global range (bulk, no shared memory involved).
 __device__ __forceinline__ void BulkPrefetchL2(const void* gmem_src, uint32_t bytes) {
     asm volatile("cp.async.bulk.prefetch.L2.global [%0], %1;" ::"l"(gmem_src), "r"(bytes)

@@ -12,6 +12,7 @@
 // then RMSNorm -> lm_head GEMV -> arg-max (token and position stay on the
 // device).  Kernels are launched with programmatic dependent launch, so each
 // one streams its weights into shared memory while the previous one finishes.
+#include <algorithm>
 #include <array>
 #include <climits>
 #include <cmath>
@@ -20,6 +21,7 @@
 
 #include "attention.cuh"
 #include "qgemv.cuh"
+#include "qmma.cuh"
 
 namespace mlb {
 
@@ -64,10 +66,19 @@ struct mlb_model {
     std::vector<std::array<Slot, 15>> layer;  // per layer, kinds 3..14
     float* rope_cos = nullptr;
     float* rope_sin = nullptr;
+    // Q8_0 models: every linear weight also in the R16 layout (integer-MMA GEMV)
+    void* r16 = nullptr;
+    size_t r16_bytes = 0;
+    Slot r16_lm_head;
+    std::vector<std::array<Slot, 15>> r16_layer;
 
     void* Ptr(const Slot& s) const { return s.bytes ? static_cast<char*>(arena) + s.offset : nullptr; }
     const Slot& Get(int l, int kind) const {
         return kind < 3 ? global[kind] : layer[l][kind];
+    }
+    const uint8_t* R16(int l, int kind) const {
+        const Slot& s = kind == MLB_W_LM_HEAD ? r16_lm_head : r16_layer[l][kind];
+        return static_cast<const uint8_t*>(r16) + s.offset;
     }
 };
 
@@ -144,6 +155,60 @@ size_t KindBytes(const mlb_model_config& c, int kind) {
     return 0;
 }
 
+bool IsLinear(int kind) {
+    return kind == MLB_W_LM_HEAD || kind == MLB_W_WQ || kind == MLB_W_WK || kind == MLB_W_WV ||
+           kind == MLB_W_WO || kind == MLB_W_GATE || kind == MLB_W_UP || kind == MLB_W_DOWN;
+}
+
+void LinearShape(const mlb_model_config& c, int kind, int& rows, int& cols) {
+    const int qd = c.n_heads * c.head_dim, kd = c.n_kv_heads * c.head_dim;
+    switch (kind) {
+        case MLB_W_LM_HEAD: rows = c.vocab_size; cols = c.dim; break;
+        case MLB_W_WQ: rows = qd; cols = c.dim; break;
+        case MLB_W_WK: case MLB_W_WV: rows = kd; cols = c.dim; break;
+        case MLB_W_WO: rows = c.dim; cols = qd; break;
+        case MLB_W_GATE: case MLB_W_UP: rows = c.hidden_dim; cols = c.dim; break;
+        default: rows = c.dim; cols = c.hidden_dim; break;  // MLB_W_DOWN
+    }
+}
+
+void RepackOne(mlb_model* m, DeviceContext& c, int l, int kind) {
+    int rows = 0, cols = 0;
+    LinearShape(m->cfg, kind, rows, cols);
+    const auto& src = m->Get(l, kind);
+    LaunchRepackQ80R16(c, m->Ptr(src), rows, cols, const_cast<uint8_t*>(m->R16(l, kind)));
+}
+
+// Q8_0 models keep an R16 copy of every linear weight for the integer-MMA GEMV.
+void PrepareR16(mlb_model* m, DeviceContext& c) {
+    if (m->cfg.weight_type != MLB_Q8_0 || m->r16) return;
+    // Every K must leave room for a two-stage ring of whole 16-row tiles.
+    const int kmax = std::max(m->cfg.dim, std::max(m->cfg.hidden_dim, m->cfg.n_heads * m->cfg.head_dim));
+    const size_t need = QmmaSmem::Bytes(1, (kmax + 31) / 32, 2 * ((kmax + 31) / 32) * kR16Chunk, 2,
+                                        kmax);
+    if (need + 4096 > static_cast<size_t>(c.max_smem_optin)) return;
+    size_t off = 0;
+    auto slot = [&](int kind) {
+        int rows = 0, cols = 0;
+        LinearShape(m->cfg, kind, rows, cols);
+        mlb_model::Slot s;
+        s.offset = off;
+        s.bytes = R16Bytes(rows, cols);
+        off += Align256(s.bytes);
+        return s;
+    };
+    m->r16_lm_head = slot(MLB_W_LM_HEAD);
+    m->r16_layer.resize(m->cfg.n_layers);
+    const int kinds[] = {MLB_W_WQ, MLB_W_WK, MLB_W_WV, MLB_W_WO, MLB_W_GATE, MLB_W_UP, MLB_W_DOWN};
+    for (int l = 0; l < m->cfg.n_layers; ++l)
+        for (int k : kinds) m->r16_layer[l][k] = slot(k);
+    m->r16_bytes = off;
+    CheckCuda(cudaMallocAsync(&m->r16, off, c.stream), "cudaMallocAsync(R16 weights)");
+    RepackOne(m, c, -1, MLB_W_LM_HEAD);
+    for (int l = 0; l < m->cfg.n_layers; ++l)
+        for (int k : kinds) RepackOne(m, c, l, k);
+}
+
 // Captures one token step on the library stream.
 void CaptureStep(mlb_session* s, DeviceContext& c) {
     mlb_model* m = s->model;
@@ -155,6 +220,22 @@ void CaptureStep(mlb_session* s, DeviceContext& c) {
     int* next = s->state + 2;
     int* status = s->state + 3;
     cudaStream_t st = c.stream;
+    const bool r16 = m->r16 != nullptr;
+    // Plans and launches one GEMV step: integer-MMA over R16 weights for Q8_0
+    // models, the bulk-copy SIMT GEMV over GGUF blocks otherwise.
+    auto gemv = [&](GemvParams& p, bool dual, int pro, int epi, const char* what) {
+        GemvPlan plan = r16 ? PlanQmma(p, 1, dual, c.sm_count, c.max_smem_optin, 1, kRingBudget)
+                            : PlanGemv(p, qt, 1, dual, c.sm_count, c.max_smem_optin, 1, kRingBudget);
+        Require(plan.ok, "mlb_session", std::string(what) + " shape not supported by the GEMV",
+                MLB_ERR_UNSUPPORTED);
+        if (epi == kEpiArgmax)
+            Require(plan.grid <= 4 * c.sm_count, "mlb_session", "arg-max partial buffer too small");
+        if (r16) LaunchQmmaDecode(pro, epi, p, plan, st);
+        else LaunchGemvDecode(qt, pro, epi, p, plan, st);
+    };
+    auto WL = [&](int l, int kind) {
+        return r16 ? m->R16(l, kind) : static_cast<const uint8_t*>(m->Ptr(m->Get(l, kind)));
+    };
 
     CheckCuda(cudaStreamBeginCapture(st, cudaStreamCaptureModeThreadLocal), "cudaStreamBeginCapture");
     try {
@@ -162,7 +243,7 @@ void CaptureStep(mlb_session* s, DeviceContext& c) {
                static_cast<const float*>(m->Ptr(m->global[MLB_W_EMBEDDING])), cf.vocab_size,
                cf.dim, const_cast<const int*>(s->hist), const_cast<const int*>(pos), s->x, status);
         for (int l = 0; l < cf.n_layers; ++l) {
-            auto W = [&](int kind) { return static_cast<const uint8_t*>(m->Ptr(m->Get(l, kind))); };
+            auto W = [&](int kind) { return WL(l, kind); };
             auto F = [&](int kind) { return static_cast<const float*>(m->Ptr(m->Get(l, kind))); };
             // 1. RMSNorm + QKV + bias
             {
@@ -178,9 +259,7 @@ void CaptureStep(mlb_session* s, DeviceContext& c) {
                 p.norm_w = F(MLB_W_ATTN_NORM);
                 p.eps = cf.rms_norm_eps;
                 p.status = status;
-                GemvPlan plan = PlanGemv(p, qt, 1, false, c.sm_count, c.max_smem_optin, 1, kRingBudget);
-                Require(plan.ok, "mlb_session", "QKV shape not supported by the GEMV", MLB_ERR_UNSUPPORTED);
-                LaunchGemvDecode(qt, kProRmsNorm, kEpiStore, p, plan, st);
+                gemv(p, false, kProRmsNorm, kEpiStore, "QKV");
             }
             // 2. RoPE + KV write + split-K attention
             {
@@ -228,10 +307,8 @@ void CaptureStep(mlb_session* s, DeviceContext& c) {
                 p.head_dim = cf.head_dim;
                 p.chunks = s->chunks;
                 p.status = status;
-                GemvPlan plan = PlanGemv(p, qt, 1, false, c.sm_count, c.max_smem_optin, 1, kRingBudget);
-                Require(plan.ok, "mlb_session", "O-projection shape not supported", MLB_ERR_UNSUPPORTED);
-                LaunchGemvDecode(qt, s->chunks > 1 ? kProAttnMerge : kProPlain, kEpiResidual, p,
-                                 plan, st);
+                gemv(p, false, s->chunks > 1 ? kProAttnMerge : kProPlain, kEpiResidual,
+                     "O-projection");
             }
             // 4. RMSNorm + gate/up + SwiGLU
             {
@@ -246,9 +323,7 @@ void CaptureStep(mlb_session* s, DeviceContext& c) {
                 p.norm_w = F(MLB_W_FFN_NORM);
                 p.eps = cf.rms_norm_eps;
                 p.status = status;
-                GemvPlan plan = PlanGemv(p, qt, 1, true, c.sm_count, c.max_smem_optin, 1, kRingBudget);
-                Require(plan.ok, "mlb_session", "FFN shape not supported", MLB_ERR_UNSUPPORTED);
-                LaunchGemvDecode(qt, kProRmsNorm, kEpiSwiglu, p, plan, st);
+                gemv(p, true, kProRmsNorm, kEpiSwiglu, "FFN");
             }
             // 5. down + residual
             {
@@ -262,9 +337,7 @@ void CaptureStep(mlb_session* s, DeviceContext& c) {
                 p.residual = s->xmid;
                 p.res_stride = cf.dim;
                 p.status = status;
-                GemvPlan plan = PlanGemv(p, qt, 1, false, c.sm_count, c.max_smem_optin, 1, kRingBudget);
-                Require(plan.ok, "mlb_session", "down-projection shape not supported", MLB_ERR_UNSUPPORTED);
-                LaunchGemvDecode(qt, kProPlain, kEpiResidual, p, plan, st);
+                gemv(p, false, kProPlain, kEpiResidual, "down-projection");
             }
         }
         // final RMSNorm + lm_head + arg-max
@@ -272,8 +345,7 @@ void CaptureStep(mlb_session* s, DeviceContext& c) {
             GemvParams p = {};
             p.K = cf.dim;
             p.nseg = 1;
-            p.seg[0] = GemvSeg{static_cast<const uint8_t*>(m->Ptr(m->global[MLB_W_LM_HEAD])),
-                               nullptr, cf.vocab_size, 0, 0, 0};
+            p.seg[0] = GemvSeg{WL(-1, MLB_W_LM_HEAD), nullptr, cf.vocab_size, 0, 0, 0};
             p.x = s->x;
             p.y = s->logits;
             p.y_stride = cf.vocab_size;
@@ -287,10 +359,7 @@ void CaptureStep(mlb_session* s, DeviceContext& c) {
             p.am_hist = s->hist;
             p.am_gen_from = gen_from;
             p.status = status;
-            GemvPlan plan = PlanGemv(p, qt, 1, false, c.sm_count, c.max_smem_optin, 1, kRingBudget);
-            Require(plan.ok, "mlb_session", "lm_head shape not supported", MLB_ERR_UNSUPPORTED);
-            Require(plan.grid <= 4 * c.sm_count, "mlb_session", "arg-max partial buffer too small");
-            LaunchGemvDecode(qt, kProRmsNorm, kEpiArgmax, p, plan, st);
+            gemv(p, false, kProRmsNorm, kEpiArgmax, "lm_head");
         }
     } catch (...) {
         cudaGraph_t g = nullptr;
@@ -384,6 +453,7 @@ int mlb_model_destroy(mlb_model* model) {
         DeviceContext& c = Ctx(model->device);
         CheckCuda(cudaStreamSynchronize(c.stream), "cudaStreamSynchronize");
         if (model->arena) CheckCuda(cudaFreeAsync(model->arena, c.stream), "cudaFreeAsync");
+        if (model->r16) CheckCuda(cudaFreeAsync(model->r16, c.stream), "cudaFreeAsync");
         delete model;
     });
 }
@@ -418,6 +488,7 @@ int mlb_model_set_weight(mlb_model* model, int layer, int kind, const void* src,
                                   src_is_host ? cudaMemcpyHostToDevice : cudaMemcpyDeviceToDevice,
                                   c.stream),
                   "cudaMemcpyAsync(weight)");
+        if (model->r16 && IsLinear(kind)) RepackOne(model, c, layer, kind);
         if (src_is_host) CheckCuda(cudaStreamSynchronize(c.stream), "cudaStreamSynchronize");
     });
 }
@@ -463,6 +534,7 @@ int mlb_session_create(mlb_model* model, mlb_session** session) {
         CheckCuda(cudaMemsetAsync(s->state, 0, 256, c.stream), "cudaMemsetAsync");
         CheckCuda(cudaMemsetAsync(s->hist, 0, size_t(cf.max_seq_len + 1) * 4, c.stream),
                   "cudaMemsetAsync");
+        PrepareR16(model, c);
         CheckCuda(cudaStreamSynchronize(c.stream), "cudaStreamSynchronize");
         CaptureStep(s.get(), c);
         *session = s.release();

@@ -44,7 +44,10 @@ GemvPlan PlanGemv(GemvParams& p, int qtype, int M, bool dual, int sm_count, int 
     p.total_tiles = total;
     const int part_bytes = (R * p.rowbytes + 15) / 16 * 16;
     p.stage_bytes = dual ? 2 * part_bytes : part_bytes;
-    plan.smem = GemvSmem::Bytes(M, p.nb, p.stage_bytes);
+    p.aux_floats = 0;
+    if (p.norm_w) p.aux_floats = p.K;
+    if (p.part_ml) p.aux_floats = p.n_heads * p.chunks * (p.head_dim + 2);
+    plan.smem = GemvSmem::Bytes(M, p.nb, p.stage_bytes, p.aux_floats);
     if (plan.smem + 4096 > static_cast<size_t>(max_smem)) return plan;
     plan.grid = std::max(1, std::min(total, sm_count * ctas_per_sm));
     plan.ok = true;
@@ -152,7 +155,7 @@ void QuantLinear(const char* caller, int device, int qtype, const float* x, cons
         p.y_stride = out_features;
         GemvPlan plan;
         for (;;) {
-            plan = PlanGemv(p, qtype, M, false, c.sm_count, c.max_smem_optin, 2);
+            plan = PlanGemv(p, qtype, M, false, c.sm_count, c.max_smem_optin, 3);
             if (plan.ok || M == 1) break;
             M = (M + 1) / 2;
             p = GemvParams{};

@@ -25,6 +25,7 @@ constexpr int kGemvWarps = kGemvThreads / 32;
 constexpr int kGemvMaxM = 8;
 constexpr int kGemvMaxTileRows = 64;
 constexpr int kGemvStages = 4;
+constexpr int kGemvMaxWarps = 16;
 
 template <int QT>
 struct QTraits;
@@ -78,6 +79,8 @@ struct GemvParams {
     GemvSeg seg[3];   // kEpiSwiglu: seg[0] = gate, seg[1] = up (same tiling)
     int total_tiles;
     int stage_bytes;
+    int aux_floats;   // shared floats for norm weights or attention partials
+    int nstages;      // integer-MMA kernel: ring stages
     // prologue
     const float* norm_w;
     float eps;
@@ -185,12 +188,14 @@ __device__ __forceinline__ void BlockDot(const uint8_t* blk, const float* xk, in
 
 namespace mlb {
 
-// Shared-memory carve-up of the GEMV kernel.
+// Shared-memory carve-up of the GEMV kernel: weight ring | mbarriers | x rows
+// [M][kpad] | aux (norm weights or attention partials) | partial sums.
 struct GemvSmem {
     static __host__ __device__ int XFloats(int M, int nb) { return M * nb * 32; }
-    static __host__ __device__ size_t Bytes(int M, int nb, int stage_bytes) {
-        return size_t(kGemvStages) * stage_bytes + 16 * kGemvStages +
-               size_t(XFloats(M, nb)) * 4 + 2ull * kGemvMaxTileRows * kGemvMaxM * 2 * 4 + 64;
+    static __host__ __device__ size_t RedBytes() { return 2ull * kGemvMaxTileRows * kGemvMaxM * 2 * 4; }
+    static __host__ __device__ size_t Bytes(int M, int nb, int stage_bytes, int aux_floats) {
+        return size_t(kGemvStages) * stage_bytes + 16 * kGemvStages + size_t(XFloats(M, nb)) * 4 +
+               size_t((aux_floats + 3) & ~3) * 4 + RedBytes() + 64;
     }
 };
 
@@ -249,6 +254,139 @@ __device__ __forceinline__ void CopyTail(const GemvParams& p, const TileRef& tr,
     }
 }
 
+// First arg-max over the rows of all CTAs: each CTA reduces its candidates,
+// the last CTA to arrive reduces the CTAs' results and writes the token (and
+// the token history / position when given).  No CTA waits on another.
+__device__ __forceinline__ void ArgmaxFinish(const GemvParams& p, float best_val, int best_idx) {
+    const int tid = threadIdx.x;
+    // CTA-level first-max, then the last CTA to finish reduces all CTAs.
+    __shared__ float sval[512];
+    __shared__ int sidx[512];
+    __shared__ bool last;
+    sval[tid] = best_val;
+    sidx[tid] = best_idx;
+    __syncthreads();
+    for (int o = blockDim.x / 2; o > 0; o >>= 1) {
+        if (tid < o) {
+            float ov = sval[tid + o];
+            int oi = sidx[tid + o];
+            if (ov > sval[tid] || (ov == sval[tid] && oi < sidx[tid])) {
+                sval[tid] = ov;
+                sidx[tid] = oi;
+            }
+        }
+        __syncthreads();
+    }
+    if (tid == 0) {
+        p.am_val[blockIdx.x] = sval[0];
+        p.am_idx[blockIdx.x] = sidx[0];
+        __threadfence();
+        unsigned prev = atomicAdd(p.am_counter, 1u);
+        last = (prev == gridDim.x - 1);
+    }
+    __syncthreads();
+    if (last) {
+        __threadfence();
+        float bv = -INFINITY;
+        int bi = 0x7fffffff;
+        for (int c = tid; c < gridDim.x; c += blockDim.x) {
+            float v = __ldcg(&p.am_val[c]);
+            int i = __ldcg(&p.am_idx[c]);
+            if (v > bv || (v == bv && i < bi)) {
+                bv = v;
+                bi = i;
+            }
+        }
+        sval[tid] = bv;
+        sidx[tid] = bi;
+        __syncthreads();
+        for (int o = blockDim.x / 2; o > 0; o >>= 1) {
+            if (tid < o) {
+                float ov = sval[tid + o];
+                int oi = sidx[tid + o];
+                if (ov > sval[tid] || (ov == sval[tid] && oi < sidx[tid])) {
+                    sval[tid] = ov;
+                    sidx[tid] = oi;
+                }
+            }
+            __syncthreads();
+        }
+        if (tid == 0) {
+            const int tok = sidx[0] == 0x7fffffff ? 0 : sidx[0];
+            *p.am_token = tok;
+            if (p.am_pos) {
+                const int ps = *p.am_pos;
+                if (p.am_hist && ps + 1 >= *p.am_gen_from) p.am_hist[ps + 1] = tok;
+                *p.am_pos = ps + 1;
+            }
+            *p.am_counter = 0;
+        }
+    }
+}
+
+// Stages x (M rows, RMS-normalised or merged from attention partials) into
+// shared memory as rows of kpad floats, zero padded.  Every global read is an
+// asynchronous copy issued before any is waited on, so the prologue costs one
+// memory round trip.  Ends with a CTA barrier.
+template <int M, int PRO>
+__device__ __forceinline__ void StageGemvX(const GemvParams& p, float* xs, float* aux, int kpad) {
+    const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
+    if constexpr (PRO == kProAttnMerge) {
+        const int nml = p.n_heads * p.chunks * 2;
+        StageFloats(aux, p.part_ml, nml);
+        StageFloats(aux + nml, p.part_o, p.n_heads * p.chunks * p.head_dim);
+        CpAsyncWaitAll();
+        __syncthreads();
+        // x[k] for k = h*head_dim + d: merge of the split-K partial softmax.
+        for (int k = tid; k < kpad; k += blockDim.x) {
+            float v = 0.0f;
+            if (k < p.K) {
+                const int h = k / p.head_dim, d = k - h * p.head_dim;
+                const float* ml = aux + h * p.chunks * 2;
+                const float* po = aux + nml + h * p.chunks * p.head_dim + d;
+                float mx = -INFINITY;
+                for (int c = 0; c < p.chunks; ++c) mx = fmaxf(mx, ml[2 * c]);
+                float num = 0.0f, den = 0.0f;
+                for (int c = 0; c < p.chunks; ++c) {
+                    const float mc = ml[2 * c];
+                    if (mc == -INFINITY) continue;
+                    const float wgt = expf(mc - mx);
+                    den = fmaf(wgt, ml[2 * c + 1], den);
+                    num = fmaf(wgt, po[c * p.head_dim], num);
+                }
+                v = den > 0.0f ? num / den : 0.0f;
+            }
+            xs[k] = v;
+        }
+    } else {
+        for (int m = 0; m < M; ++m) StageFloats(xs + m * kpad, p.x + size_t(m) * p.K, p.K);
+        if constexpr (PRO == kProRmsNorm) StageFloats(aux, p.norm_w, p.K);
+        for (int m = 0; m < M; ++m)
+            for (int k = p.K + tid; k < kpad; k += blockDim.x) xs[m * kpad + k] = 0.0f;
+        CpAsyncWaitAll();
+        __syncthreads();
+        if constexpr (PRO == kProRmsNorm) {
+            __shared__ float wsum[kGemvMaxWarps];
+            for (int m = 0; m < M; ++m) {
+                float* xr = xs + m * kpad;
+                float ss = 0.0f;
+                for (int k = tid; k < p.K; k += blockDim.x) ss = fmaf(xr[k], xr[k], ss);
+                ss = WarpSum(ss);
+                if (lane == 0) wsum[warp] = ss;
+                __syncthreads();
+                float tot = 0.0f;
+#pragma unroll
+                for (int w = 0; w < kGemvMaxWarps; ++w) tot += wsum[w];
+                __syncthreads();
+                const float scale = 1.0f / sqrtf(tot / static_cast<float>(p.K) + p.eps);
+                for (int k = tid; k < p.K; k += blockDim.x) xr[k] = xr[k] * scale * aux[k];
+            }
+        }
+    }
+    __syncthreads();
+
+}
+
 template <int QT, int M, int PRO, int EPI>
 __global__ void __launch_bounds__(kGemvThreads) GemvKernel(const GemvParams p) {
     constexpr bool kDual = (EPI == kEpiSwiglu);
@@ -259,7 +397,8 @@ __global__ void __launch_bounds__(kGemvThreads) GemvKernel(const GemvParams p) {
     float* xs = reinterpret_cast<float*>(smem + size_t(kGemvStages) * p.stage_bytes +
                                          16 * kGemvStages);
     const int kpad = p.nb * 32;
-    float* red = xs + M * kpad;  // [2][kGemvMaxTileRows][M][2]
+    float* aux = xs + M * kpad;
+    float* red = aux + ((p.aux_floats + 3) & ~3);  // [2][kGemvMaxTileRows][M][2]
 
     const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
     const int ntiles = p.total_tiles;
@@ -283,57 +422,7 @@ __global__ void __launch_bounds__(kGemvThreads) GemvKernel(const GemvParams p) {
     GridDepWait();
     GridDepLaunch();
 
-    // ---- prologue: x (normalised / merged) into shared memory, zero padded
-    if constexpr (PRO == kProAttnMerge) {
-        // x[k] for k = h*head_dim + d: merge of the split-K partial softmax.
-        for (int k = tid; k < kpad; k += kGemvThreads) {
-            float v = 0.0f;
-            if (k < p.K) {
-                int h = k / p.head_dim, d = k - h * p.head_dim;
-                const float* ml = p.part_ml + size_t(h) * p.chunks * 2;
-                float mx = -INFINITY;
-                for (int c = 0; c < p.chunks; ++c) mx = fmaxf(mx, ml[2 * c]);
-                float num = 0.0f, den = 0.0f;
-                for (int c = 0; c < p.chunks; ++c) {
-                    float mc = ml[2 * c];
-                    if (mc == -INFINITY) continue;
-                    float wgt = __expf(mc - mx);
-                    den = fmaf(wgt, ml[2 * c + 1], den);
-                    num = fmaf(wgt, p.part_o[(size_t(h) * p.chunks + c) * p.head_dim + d], num);
-                }
-                v = num / den;
-            }
-            xs[k] = v;
-        }
-    } else {
-        for (int m = 0; m < M; ++m) {
-            const float* xr = p.x + size_t(m) * p.K;
-            float scale = 1.0f;
-            if constexpr (PRO == kProRmsNorm) {
-                float ss = 0.0f;
-                for (int k = tid; k < p.K; k += kGemvThreads) ss = fmaf(xr[k], xr[k], ss);
-                ss = WarpSum(ss);
-                __shared__ float wsum[kGemvWarps];
-                if (lane == 0) wsum[warp] = ss;
-                __syncthreads();
-                float tot = 0.0f;
-#pragma unroll
-                for (int w = 0; w < kGemvWarps; ++w) tot += wsum[w];
-                __syncthreads();
-                tot = tot / static_cast<float>(p.K);
-                scale = 1.0f / sqrtf(tot + p.eps);
-            }
-            for (int k = tid; k < kpad; k += kGemvThreads) {
-                float v = 0.0f;
-                if (k < p.K) {
-                    v = xr[k];
-                    if constexpr (PRO == kProRmsNorm) v = v * scale * p.norm_w[k];
-                }
-                xs[m * kpad + k] = v;
-            }
-        }
-    }
-    __syncthreads();
+    StageGemvX<M, PRO>(p, xs, aux, kpad);
 
     float best_val = -INFINITY;
     int best_idx = 0x7fffffff;
@@ -364,11 +453,17 @@ __global__ void __launch_bounds__(kGemvThreads) GemvKernel(const GemvParams p) {
             for (int m = 0; m < M; ++m) acc[m] = acc2[m] = 0.0f;
             const uint8_t* row = stage + size_t(r) * p.rowbytes;
             const uint8_t* row2 = row + p.stage_bytes / 2;
-            for (int g = part; g < groups; g += P) {
-                const int b = g * 4 + blk_in_group;
-                if (b < p.nb) {
-                    BlockDot<QT, M>(row + b * kBB, xs + b * 32, kpad, sub, acc);
-                    if constexpr (kDual) BlockDot<QT, M>(row2 + b * kBB, xs + b * 32, kpad, sub, acc2);
+            // two block groups per iteration: independent loads in flight
+            for (int g = part; g < groups; g += 2 * P) {
+                const int b0 = g * 4 + blk_in_group;
+                const int b1 = b0 + 4 * P;
+                if (b0 < p.nb) {
+                    BlockDot<QT, M>(row + b0 * kBB, xs + b0 * 32, kpad, sub, acc);
+                    if constexpr (kDual) BlockDot<QT, M>(row2 + b0 * kBB, xs + b0 * 32, kpad, sub, acc2);
+                }
+                if (b1 < p.nb) {
+                    BlockDot<QT, M>(row + b1 * kBB, xs + b1 * 32, kpad, sub, acc);
+                    if constexpr (kDual) BlockDot<QT, M>(row2 + b1 * kBB, xs + b1 * 32, kpad, sub, acc2);
                 }
             }
 #pragma unroll
@@ -432,71 +527,7 @@ __global__ void __launch_bounds__(kGemvThreads) GemvKernel(const GemvParams p) {
         }
     }
 
-    if constexpr (EPI == kEpiArgmax) {
-        // CTA-level first-max, then the last CTA to finish reduces all CTAs.
-        __shared__ float sval[kGemvThreads];
-        __shared__ int sidx[kGemvThreads];
-        __shared__ bool last;
-        sval[tid] = best_val;
-        sidx[tid] = best_idx;
-        __syncthreads();
-        for (int o = kGemvThreads / 2; o > 0; o >>= 1) {
-            if (tid < o) {
-                float ov = sval[tid + o];
-                int oi = sidx[tid + o];
-                if (ov > sval[tid] || (ov == sval[tid] && oi < sidx[tid])) {
-                    sval[tid] = ov;
-                    sidx[tid] = oi;
-                }
-            }
-            __syncthreads();
-        }
-        if (tid == 0) {
-            p.am_val[blockIdx.x] = sval[0];
-            p.am_idx[blockIdx.x] = sidx[0];
-            __threadfence();
-            unsigned prev = atomicAdd(p.am_counter, 1u);
-            last = (prev == gridDim.x - 1);
-        }
-        __syncthreads();
-        if (last) {
-            __threadfence();
-            float bv = -INFINITY;
-            int bi = 0x7fffffff;
-            for (int c = tid; c < gridDim.x; c += kGemvThreads) {
-                float v = __ldcg(&p.am_val[c]);
-                int i = __ldcg(&p.am_idx[c]);
-                if (v > bv || (v == bv && i < bi)) {
-                    bv = v;
-                    bi = i;
-                }
-            }
-            sval[tid] = bv;
-            sidx[tid] = bi;
-            __syncthreads();
-            for (int o = kGemvThreads / 2; o > 0; o >>= 1) {
-                if (tid < o) {
-                    float ov = sval[tid + o];
-                    int oi = sidx[tid + o];
-                    if (ov > sval[tid] || (ov == sval[tid] && oi < sidx[tid])) {
-                        sval[tid] = ov;
-                        sidx[tid] = oi;
-                    }
-                }
-                __syncthreads();
-            }
-            if (tid == 0) {
-                const int tok = sidx[0] == 0x7fffffff ? 0 : sidx[0];
-                *p.am_token = tok;
-                if (p.am_pos) {
-                    const int ps = *p.am_pos;
-                    if (p.am_hist && ps + 1 >= *p.am_gen_from) p.am_hist[ps + 1] = tok;
-                    *p.am_pos = ps + 1;
-                }
-                *p.am_counter = 0;
-            }
-        }
-    }
+    if constexpr (EPI == kEpiArgmax) ArgmaxFinish(p, best_val, best_idx);
 }
 
 // Host-side planning of a GEMV launch: tile sizes, stage size and grid.

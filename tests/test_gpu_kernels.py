@@ -312,3 +312,57 @@ def test_attention_validation(mlb, gpu):
     assert st == capi.MLB_ERR_OUT_OF_RANGE
     st = mlb.raw("mlb_attention_decode", gpu, q.ptr, kc.ptr, kc.ptr, 1, 4, 0, 1, 3, 2, 64, q.ptr)
     assert st == capi.MLB_ERR_INVALID_ARGUMENT and "divisible" in mlb.last_error()
+
+
+R16_SHAPES = [(5, 13), (16, 32), (33, 33), (7, 176), (896, 896), (4864, 896), (896, 4864),
+              (151936, 896)]
+
+
+@pytest.mark.parametrize("n,k", R16_SHAPES)
+@pytest.mark.parametrize("m", [1, 2, 3, 8])
+def test_q80_r16_integer_mma_linear(mlb, gpu, oracle, n, k, m):
+    """Prepared (R16) Q8_0 weights through the integer tensor-core GEMV."""
+    if n == 151936 and m not in (1, 8):
+        pytest.skip("lm_head shape covered at M = 1 and 8")
+    blocks = bench_blocks(oracle, Q80, n, k) if (n, k) in BENCH_SHAPES else oracle.quantize(
+        Q80, oracle.normal(n * k, 2, STREAM_W + 3000 + n + k, 0.02).reshape(n, k))
+    x = oracle.normal(m * k, 2, STREAM_X + 3000 + n + k, 1.0).reshape(m, k)
+    x[0, :7] *= np.float32(1e-3)   # blocks with a wide dynamic range
+    if k > 40:
+        x[-1, 32:64] = 0.0         # an all-zero block
+    expect = oracle.linear(Q80, x, blocks, n)
+    wd = DeviceArray.from_host(mlb, gpu, blocks)
+    r16 = DeviceArray(mlb, gpu, mlb.dll.mlb_r16_bytes(n, k), np.uint8)
+    mlb.call("mlb_q80_repack_r16", gpu, wd.ptr, n, k, r16.ptr)
+    xd = DeviceArray.from_host(mlb, gpu, x)
+    yd = DeviceArray(mlb, gpu, (m, n))
+    bias = oracle.normal(n, 2, 4000 + n, 0.1)
+    bd = DeviceArray.from_host(mlb, gpu, bias)
+    mlb.call("mlb_q80_linear_r16", gpu, xd.ptr, r16.ptr, m, k, n, bd.ptr, yd.ptr)
+    assert_close(yd.download(), expect + bias, LIN_TOL, f"R16 [{n},{k}] M={m}")
+
+
+def test_q80_r16_layout(mlb, gpu, oracle):
+    """The R16 copy holds the same quants and scales, regrouped."""
+    n, k = 20, 70
+    blocks = oracle.quantize(Q80, oracle.normal(n * k, 2, 5000, 0.02).reshape(n, k))
+    nb = 3
+    wd = DeviceArray.from_host(mlb, gpu, blocks)
+    size = mlb.dll.mlb_r16_bytes(n, k)
+    assert size == 2 * nb * 544
+    r16 = DeviceArray(mlb, gpu, size, np.uint8)
+    mlb.call("mlb_q80_repack_r16", gpu, wd.ptr, n, k, r16.ptr)
+    got = r16.download().reshape(2, nb, 544)
+    g = blocks.reshape(n, nb, 34)
+    for r in range(32):
+        t, i = divmod(r, 16)
+        for b in range(nb):
+            chunk = got[t, b]
+            swz = (i >> 2) & 1
+            q = np.concatenate([chunk[32 * i + 16 * (0 ^ swz):32 * i + 16 * (0 ^ swz) + 16],
+                                chunk[32 * i + 16 * (1 ^ swz):32 * i + 16 * (1 ^ swz) + 16]])
+            d = chunk[512 + 2 * i:514 + 2 * i]
+            if r < n:
+                assert np.array_equal(q, g[r, b, 2:]) and np.array_equal(d, g[r, b, :2])
+            else:
+                assert not q.any() and not d.any()
