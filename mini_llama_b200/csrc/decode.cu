@@ -182,11 +182,16 @@ void RepackOne(mlb_model* m, DeviceContext& c, int l, int kind) {
 // Q8_0 models keep an R16 copy of every linear weight for the integer-MMA GEMV.
 void PrepareR16(mlb_model* m, DeviceContext& c) {
     if (m->cfg.weight_type != MLB_Q8_0 || m->r16) return;
-    // Every K must leave room for a two-stage ring of whole 16-row tiles.
-    const int kmax = std::max(m->cfg.dim, std::max(m->cfg.hidden_dim, m->cfg.n_heads * m->cfg.head_dim));
-    const size_t need = QmmaSmem::Bytes(1, (kmax + 31) / 32, 2 * ((kmax + 31) / 32) * kR16Chunk, 2,
-                                        kmax);
-    if (need + 4096 > static_cast<size_t>(c.max_smem_optin)) return;
+    // Every GEMV step must leave room for a two-stage ring of whole 16-row
+    // tiles (gate/up hold two tiles per stage).
+    auto need = [](int k, int tiles_per_stage, int aux) {
+        const int nb = (k + 31) / 32;
+        return QmmaSmem::Bytes(1, nb, tiles_per_stage * nb * kR16Chunk, 2, aux);
+    };
+    const mlb_model_config& cf = m->cfg;
+    const size_t worst = std::max({need(cf.dim, 2, cf.dim), need(cf.hidden_dim, 1, 0),
+                                   need(cf.n_heads * cf.head_dim, 1, cf.n_heads * 64 * (cf.head_dim + 2))});
+    if (worst + 4096 > static_cast<size_t>(c.max_smem_optin)) return;
     size_t off = 0;
     auto slot = [&](int kind) {
         int rows = 0, cols = 0;
