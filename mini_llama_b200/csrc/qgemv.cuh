@@ -376,7 +376,7 @@ __device__ __forceinline__ void StageGemvX(const GemvParams& p, float* xs, float
                 __syncthreads();
                 float tot = 0.0f;
 #pragma unroll
-                for (int w = 0; w < kGemvMaxWarps; ++w) tot += wsum[w];
+                for (int w = 0; w < (blockDim.x >> 5); ++w) tot += wsum[w];
                 __syncthreads();
                 const float scale = 1.0f / sqrtf(tot / static_cast<float>(p.K) + p.eps);
                 for (int k = tid; k < p.K; k += blockDim.x) xr[k] = xr[k] * scale * aux[k];
