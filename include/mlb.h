@@ -252,6 +252,10 @@ int mlb_session_generate(mlb_session* session, const int* prompt, int n_prompt, 
 int mlb_session_decode_device(mlb_session* session, int* tokens, int start_pos, int n_steps);
 /* Device pointer of the last logits (vocab floats). */
 int mlb_session_logits(mlb_session* session, const float** logits);
+/* Which GEMV the session's graph uses: 1 = integer tensor-core GEMV over R16
+ * weights (Q8_0 models whose shapes fit), 0 = bulk-copy SIMT GEMV over the
+ * GGUF blocks. */
+int mlb_session_gemv_path(mlb_session* session, int* path);
 /* Device pointers of the session KV cache. */
 int mlb_session_kv_cache(mlb_session* session, float** key_cache, float** value_cache);
 

@@ -96,6 +96,7 @@ SIGNATURES = {
     "mlb_session_generate": (_i, [_vp, _vp, _i, _i, _i, _vp]),
     "mlb_session_decode_device": (_i, [_vp, _vp, _i, _i]),
     "mlb_session_logits": (_i, [_vp, _pp]),
+    "mlb_session_gemv_path": (_i, [_vp, _pi]),
     "mlb_session_kv_cache": (_i, [_vp, _pp, _pp]),
 }
 

@@ -180,7 +180,7 @@ void RepackOne(mlb_model* m, DeviceContext& c, int l, int kind) {
 }
 
 // Q8_0 models keep an R16 copy of every linear weight for the integer-MMA GEMV.
-void PrepareR16(mlb_model* m, DeviceContext& c) {
+void PrepareR16(mlb_model* m, DeviceContext& c, int chunks) {
     if (m->cfg.weight_type != MLB_Q8_0 || m->r16) return;
     // Every GEMV step must leave room for a two-stage ring of whole 16-row
     // tiles (gate/up hold two tiles per stage).
@@ -190,7 +190,7 @@ void PrepareR16(mlb_model* m, DeviceContext& c) {
     };
     const mlb_model_config& cf = m->cfg;
     const size_t worst = std::max({need(cf.dim, 2, cf.dim), need(cf.hidden_dim, 1, 0),
-                                   need(cf.n_heads * cf.head_dim, 1, cf.n_heads * 64 * (cf.head_dim + 2))});
+                                   need(cf.n_heads * cf.head_dim, 1, cf.n_heads * chunks * (cf.head_dim + 2))});
     if (worst + 4096 > static_cast<size_t>(c.max_smem_optin)) return;
     size_t off = 0;
     auto slot = [&](int kind) {
@@ -539,7 +539,7 @@ int mlb_session_create(mlb_model* model, mlb_session** session) {
         CheckCuda(cudaMemsetAsync(s->state, 0, 256, c.stream), "cudaMemsetAsync");
         CheckCuda(cudaMemsetAsync(s->hist, 0, size_t(cf.max_seq_len + 1) * 4, c.stream),
                   "cudaMemsetAsync");
-        PrepareR16(model, c);
+        PrepareR16(model, c, s->chunks);
         CheckCuda(cudaStreamSynchronize(c.stream), "cudaStreamSynchronize");
         CaptureStep(s.get(), c);
         *session = s.release();
@@ -652,6 +652,13 @@ int mlb_session_logits(mlb_session* session, const float** logits) {
     return Guard([&] {
         Require(session && logits, "mlb_session_logits", "null argument");
         *logits = session->logits;
+    });
+}
+
+int mlb_session_gemv_path(mlb_session* session, int* path) {
+    return Guard([&] {
+        Require(session && path, "mlb_session_gemv_path", "null argument");
+        *path = session->model->r16 ? 1 : 0;
     });
 }
 

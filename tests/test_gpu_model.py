@@ -159,3 +159,16 @@ def test_session_rejects_bad_inputs(mlb, gpu, qwen2):
         assert st == capi.MLB_ERR_OUT_OF_RANGE
     finally:
         s.close()
+
+
+
+def test_q8_0_session_uses_integer_mma_path(mlb, gpu, qwen2):
+    """A Q8_0 model decodes through the integer-MMA GEMV over R16 weights."""
+    import ctypes
+    s = Session(qwen2)
+    try:
+        path = ctypes.c_int(-1)
+        mlb.call("mlb_session_gemv_path", s.handle, ctypes.byref(path))
+        assert path.value == 1
+    finally:
+        s.close()
