@@ -1,4 +1,5 @@
 // Decode-attention entry points (replace mini_llama include/cuda_attention.h:10-14).
+#include <algorithm>
 #include <cmath>
 
 #include "attention.cuh"
@@ -6,13 +7,13 @@
 namespace mlb {
 
 int AttnChunks(int max_npos, int batch, int n_kv, int hgroups, int sm_count) {
-    // ~128 positions per CTA (one 32-position tile per warp), but no more CTAs
-    // than about four waves of the SMs.
-    long long base = 1LL * batch * n_kv * hgroups;
-    long long by_len = (max_npos + 127) / 128;
-    long long by_sms = std::max(1LL, (4LL * sm_count + base - 1) / base);
-    long long c = std::min(by_len, by_sms);
-    return static_cast<int>(std::max(1LL, std::min(c, 1024LL)));
+    // at most kAttnChunk positions per CTA (K and V of a chunk fit in shared
+    // memory); more chunks while the grid is below about two waves of SMs
+    (void)hgroups;
+    long long c = (max_npos + kAttnChunk - 1) / kAttnChunk;
+    long long base = 1LL * batch * n_kv;
+    while (c * 2 * base <= 2LL * sm_count && c * 2 * 16 <= max_npos) c *= 2;
+    return static_cast<int>(std::max(1LL, c));
 }
 
 template <int DPL>
