@@ -170,6 +170,26 @@ int mlb_attention_decode_batched(int device, int batch, const float* q, const fl
                                  int layer, const int* positions, int max_pos, int n_heads,
                                  int n_kv_heads, int head_dim, float* out);
 
+/* The same decode attention for callers that cannot allocate device memory
+ * while decoding: for example an application in which another framework
+ * already holds all free device memory, or a thread that must not take the
+ * allocator's locks or risk the device synchronisation that freeing memory
+ * can cause.  No counterpart in the reference.
+ * The split-K partials live in one fixed 16 MiB array inside the library
+ * image, present on every device that loads the library until the process
+ * exits; a shape whose partials need more (n_heads x chunks x (head_dim + 2)
+ * floats) is rejected with MLB_ERR_UNSUPPORTED.  The first call on a device
+ * also does the library's one-time set-up for that device (its stream and the
+ * array's device address), allocating no device memory; make that first call
+ * before any stream capture.  Every call uses the same array, which keeps the
+ * last call's contents; calls whose work overlaps on the GPU race on it.  This
+ * library issues all of a device's work on one stream, so its own calls are
+ * ordered. */
+int mlb_attention_decode_noalloc(int device, const float* q, const float* key_cache,
+                                 const float* value_cache, int n_layers, int max_seq_len,
+                                 int layer, int pos, int n_heads, int n_kv_heads, int head_dim,
+                                 float* out);
+
 /* ------------------------------------------------------------ synthetic inputs
  * Seeded N(0, sigma) fill on the device, bit-identical to the host generator
  * used for fixtures (splitmix64 counter stream, Irwin-Hall sum of 12 uniform

@@ -83,6 +83,7 @@ SIGNATURES = {
     "mlb_attention_decode": (_i, [_i, _vp, _vp, _vp, _i, _i, _i, _i, _i, _i, _i, _vp]),
     "mlb_attention_decode_batched": (_i, [_i, _i, _vp, _vp, _vp, _i, _i, _i, _vp, _i, _i, _i,
                                           _i, _vp]),
+    "mlb_attention_decode_noalloc": (_i, [_i, _vp, _vp, _vp, _i, _i, _i, _i, _i, _i, _i, _vp]),
     "mlb_synth_normal": (_i, [_i, _vp, _sz, _u64, _u64, _d]),
     "mlb_model_create": (_i, [_i, ctypes.POINTER(ModelConfig), _pp]),
     "mlb_model_destroy": (_i, [_vp]),
