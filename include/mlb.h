@@ -99,6 +99,15 @@ int mlb_q41_linear(int device, const float* x, const void* w, size_t block_count
 int mlb_quant_linear(int device, int qtype, const float* x, const void* w, size_t block_count,
                      int rows, int in_features, int out_features, const float* bias, float* y);
 
+/* F32 linear and matmul: replace include/cuda_matmul.h:11-33 (CudaLinear,
+ * CudaLinearDeviceWeight, CudaLinearDeviceInput, CudaMatmul; the reference
+ * calls cublasSgemm with a new handle per call, src/cuda_matmul.cpp:118-229).
+ * mlb_f32_linear: y[rows, out] = x[rows, in] . W[out, in]^T (+ bias[out]).
+ * mlb_f32_matmul: c[m, n] = a[m, k] . b[k, n], all row-major. */
+int mlb_f32_linear(int device, const float* x, const float* w, int rows, int in_features,
+                   int out_features, const float* bias, float* y);
+int mlb_f32_matmul(int device, const float* a, const float* b, int m, int k, int n, float* c);
+
 /* Prepared Q8_0 weights ("R16" layout): the same bytes regrouped into 16-row
  * tiles of 544-byte chunks (16 x 32 int8 quants, then 16 fp16 scales), every
  * chunk 16-byte aligned.  A caller that keeps a prepared copy gets the

@@ -66,6 +66,8 @@ SIGNATURES = {
     "mlb_q40_linear": (_i, [_i, _vp, _vp, _sz, _i, _i, _i, _vp, _vp]),
     "mlb_q41_linear": (_i, [_i, _vp, _vp, _sz, _i, _i, _i, _vp, _vp]),
     "mlb_quant_linear": (_i, [_i, _i, _vp, _vp, _sz, _i, _i, _i, _vp, _vp]),
+    "mlb_f32_linear": (_i, [_i, _vp, _vp, _i, _i, _i, _vp, _vp]),
+    "mlb_f32_matmul": (_i, [_i, _vp, _vp, _i, _i, _i, _vp]),
     "mlb_r16_bytes": (_sz, [_i, _i]),
     "mlb_q80_repack_r16": (_i, [_i, _vp, _i, _i, _vp]),
     "mlb_q80_linear_r16": (_i, [_i, _vp, _vp, _i, _i, _i, _vp, _vp]),

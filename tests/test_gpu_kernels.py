@@ -366,3 +366,27 @@ def test_q80_r16_layout(mlb, gpu, oracle):
                 assert np.array_equal(q, g[r, b, 2:]) and np.array_equal(d, g[r, b, :2])
             else:
                 assert not q.any() and not d.any()
+
+
+@pytest.mark.parametrize("m,k,n", [(1, 33, 7), (3, 33, 7), (1, 896, 4864), (8, 896, 1000),
+                                   (2, 4864, 896), (1, 896, 151936)])
+def test_f32_linear(mlb, gpu, oracle, m, k, n):
+    w = oracle.normal(n * k, 6, 100 + k, 0.02).reshape(n, k)
+    x = oracle.normal(m * k, 6, 200 + k, 1.0).reshape(m, k)
+    bias = oracle.normal(n, 6, 300, 0.1)
+    wd, xd, bd = (DeviceArray.from_host(mlb, gpu, w), DeviceArray.from_host(mlb, gpu, x),
+                  DeviceArray.from_host(mlb, gpu, bias))
+    yd = DeviceArray(mlb, gpu, (m, n))
+    mlb.call("mlb_f32_linear", gpu, xd.ptr, wd.ptr, m, k, n, bd.ptr, yd.ptr)
+    ref = (x.astype(np.float64) @ w.astype(np.float64).T) + bias
+    assert_close(yd.download(), ref, 2e-4, f"f32 linear {m}x{k}x{n}")
+
+
+@pytest.mark.parametrize("m,k,n", [(3, 17, 9), (65, 130, 70), (128, 64, 128)])
+def test_f32_matmul(mlb, gpu, oracle, m, k, n):
+    a = oracle.normal(m * k, 6, 400 + k, 0.5).reshape(m, k)
+    b = oracle.normal(k * n, 6, 500 + k, 0.5).reshape(k, n)
+    ad, bd = DeviceArray.from_host(mlb, gpu, a), DeviceArray.from_host(mlb, gpu, b)
+    cd = DeviceArray(mlb, gpu, (m, n))
+    mlb.call("mlb_f32_matmul", gpu, ad.ptr, bd.ptr, m, k, n, cd.ptr)
+    assert_close(cd.download(), a.astype(np.float64) @ b.astype(np.float64), 2e-4, "f32 matmul")
