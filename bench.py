@@ -3,14 +3,17 @@
     python bench.py [--gpus N] [--steps K] [--warmup W] [--impl reference]
 
 A step decodes 128 tokens (positions 64..191 after a 64-token prompt) through
-the device session (one CUDA graph per token, token fed back on the device).
+the device session: one launch of the persistent decode kernel per step (every
+layer of every token in one cooperative kernel, tokens fed back on the
+device); --graph selects the CUDA graph per token instead.
   value  tokens/s with everything resident in HBM (CUDA events on the library
          stream, max over ranks); weights (528 MB/token) exceed the 126 MB L2,
          so no flush is needed between steps
   e2e    the same through mlb_session_generate with host buffers: the step's
          start token copied host->device and the 128 generated ids copied back
-  roofline  the dominant kernel (the Q8_0 GEMV) timed alone on the lm_head
-         shape [151936, 896]: algorithmic bytes / CUDA-event time vs measured HBM
+  roofline  the dominant kernel: the persistent decode kernel, algorithmic
+         bytes of its 128 tokens / its CUDA-event time per launch vs measured
+         HBM (graph path: the Q8_0 GEMV timed alone on the lm_head shape)
   cpu_baseline  the reference CPU implementation (RunBenchmark, built from the
          reference sources into oracle/_ref) on a bounded sample
 With N > 1 (torchrun) every GPU decodes its own sequence (replicas; weak scaling).
@@ -213,6 +216,9 @@ def run_ours(args):
     model = Model(lib, dev, QWEN2)
     model.synthesize(seed=QWEN2["seed"], tied=True)
     sess = Session(model)
+    if args.graph:
+        sess.use_persistent(False)
+    path = sess.path()
     from oracle.binding import Oracle  # only for the prompt ids (seeded generator)
     prompt = Oracle().tokens(PROMPT, QWEN2["prompt_seed"], QWEN2["vocab_size"])
     if args.no_prefill:  # profiling runs: decode from position 64 over an empty cache
@@ -281,11 +287,25 @@ def run_ours(args):
         e2e = world * NEW * args.steps / e2e_secs
 
     peaks = measured_peaks()
-    algo, launch_s = gemv_roofline(lib, dev, torch, stream)
-    achieved = algo / launch_s / 1e9
     step_bytes = sum(algorithmic_bytes_per_token(p) for p in range(PROMPT, PROMPT + new))
     step_gbs = step_bytes * args.steps / secs / 1e9 if world == 1 else None
     launches_per_token = 1 + 5 * QWEN2["n_layers"] + 1
+    if path == 2:
+        # one kernel per step; its launch time is the step time less the
+        # few-microsecond state copies around it
+        roof = {"bound": "hbm", "kernel": f"MegaDecodeKernel (persistent, {new} tokens per launch)",
+                "achieved": step_bytes * args.steps / secs / 1e9, "peak": peaks["hbm_gbs"],
+                "unit": "GB/s", "peak_source": peaks["source"], "bytes_per_launch": step_bytes,
+                "launch_us": secs / args.steps * 1e6, "traffic": committed_traffic("mega_decode")}
+        gpu_launches = args.steps
+    else:
+        algo, launch_s = gemv_roofline(lib, dev, torch, stream)
+        roof = {"bound": "hbm", "kernel": "QmmaGemvKernel<M=1> (Q8_0, R16) on [151936, 896]",
+                "achieved": algo / launch_s / 1e9, "peak": peaks["hbm_gbs"], "unit": "GB/s",
+                "peak_source": peaks["source"], "bytes_per_launch": algo,
+                "launch_us": launch_s * 1e6, "traffic": committed_traffic("qmma_lm_head")}
+        gpu_launches = launches_per_token * new * args.steps
+    roof["frac"] = roof["achieved"] / roof["peak"]
 
     sess.close()
     model.close()
@@ -313,17 +333,15 @@ def run_ours(args):
         "e2e": {"value": e2e, "unit": UNIT, "h2d_bytes_per_step": 4 + 8 + 4,
                 "d2h_bytes_per_step": NEW * 4 + 4,
                 "path": "mlb_session_generate(host start token -> host 128 token ids)"},
-        "roofline": {"bound": "hbm", "kernel": "QmmaGemvKernel<M=1> (Q8_0, R16) on [151936, 896]",
-                     "achieved": achieved, "peak": peaks["hbm_gbs"], "unit": "GB/s",
-                     "frac": achieved / peaks["hbm_gbs"], "peak_source": peaks["source"],
-                     "bytes_per_launch": algo, "launch_us": launch_s * 1e6,
-                     "traffic": committed_traffic("qmma_lm_head")},
+        "decode_path": {2: "persistent kernel", 1: "graph, integer-MMA GEMV",
+                        0: "graph, SIMT GEMV"}[path],
+        "roofline": roof,
         "step_roofline": {"bytes_per_token_avg": step_bytes / new,
                           "achieved_gbs": step_gbs,
                           "frac": (step_gbs / peaks["hbm_gbs"]) if step_gbs else None},
         "cpu_baseline": cpu,
         "clocks": clk,
-        "gpu_launches": launches_per_token * new * args.steps,
+        "gpu_launches": gpu_launches,
     }
     print(json.dumps(line), flush=True)
     return 0
@@ -339,6 +357,8 @@ def main():
     ap.add_argument("--no-e2e", action="store_true")
     ap.add_argument("--no-prefill", action="store_true",
                     help="profiling: skip the 64-token prefill (KV cache left empty)")
+    ap.add_argument("--graph", action="store_true",
+                    help="decode through the CUDA graph per token instead of the persistent kernel")
     ap.add_argument("--roofline-only", action="store_true",
                     help="time only the Q8_0 GEMV on the lm_head shape")
     ap.add_argument("--decode-tokens", type=int, default=NEW,

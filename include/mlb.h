@@ -281,10 +281,29 @@ int mlb_session_generate(mlb_session* session, const int* prompt, int n_prompt, 
 int mlb_session_decode_device(mlb_session* session, int* tokens, int start_pos, int n_steps);
 /* Device pointer of the last logits (vocab floats). */
 int mlb_session_logits(mlb_session* session, const float** logits);
-/* Which GEMV the session's graph uses: 1 = integer tensor-core GEMV over R16
- * weights (Q8_0 models whose shapes fit), 0 = bulk-copy SIMT GEMV over the
- * GGUF blocks. */
+/* Which decode path the session uses: 2 = the persistent decode kernel (one
+ * cooperative launch per generate / decode_device / forward call, integer
+ * tensor-core products over R16 weights), 1 = a CUDA graph per token whose
+ * GEMVs are the integer tensor-core GEMV over R16 weights, 0 = a CUDA graph
+ * per token with the bulk-copy SIMT GEMV over the GGUF blocks.  Q8_0 models
+ * whose shapes fit get 2, other Q8_0 models 1, Q4_0 / Q4_1 models 0. */
 int mlb_session_gemv_path(mlb_session* session, int* path);
+/* Selects (enable = 1) or leaves (enable = 0) the persistent decode kernel
+ * for this session; MLB_ERR_UNSUPPORTED when the model does not fit it.  No
+ * reference counterpart: the per-token graph stays available for
+ * comparison. */
+int mlb_session_use_persistent(mlb_session* session, int enable);
+/* Phase timeline of the persistent decode kernel (a profiling aid; no
+ * reference counterpart).  With a device buffer of `entries` uint64, later
+ * launches stamp %globaltimer (ns) at
+ *   buffer[((step * (n_layers + 1) + layer) * 12 + event) * sm_count + cta]
+ * for each CTA that takes part in the phase.  QKV: 0 wait done, 11 input
+ * normalised, 10 products stored, 1 signalled.  Attention: 2 wait done,
+ * 8 softmax.V done, 9 O-projection issued, 3 signalled.  FFN: 4 wait done,
+ * 7 input normalised, 6 down-projection issued, 5 signalled.  Layer n_layers
+ * (lm_head): 0 wait done, 1 done.  Stamps past `entries` are dropped; the
+ * buffer is not cleared.  NULL, 0 turns the timeline off. */
+int mlb_session_trace(mlb_session* session, unsigned long long* device_buffer, size_t entries);
 /* Device pointers of the session KV cache. */
 int mlb_session_kv_cache(mlb_session* session, float** key_cache, float** value_cache);
 

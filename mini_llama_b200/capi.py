@@ -100,6 +100,8 @@ SIGNATURES = {
     "mlb_session_decode_device": (_i, [_vp, _vp, _i, _i]),
     "mlb_session_logits": (_i, [_vp, _pp]),
     "mlb_session_gemv_path": (_i, [_vp, _pi]),
+    "mlb_session_use_persistent": (_i, [_vp, _i]),
+    "mlb_session_trace": (_i, [_vp, _vp, _sz]),
     "mlb_session_kv_cache": (_i, [_vp, _pp, _pp]),
 }
 

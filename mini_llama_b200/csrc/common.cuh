@@ -159,6 +159,34 @@ __device__ __forceinline__ bool MbarWait(uint64_t* bar, uint32_t parity) {
     return false;
 }
 
+__device__ __forceinline__ uint64_t GlobalTimerNs() {
+    uint64_t t;
+    asm volatile("mov.u64 %0, %%globaltimer;" : "=l"(t));
+    return t;
+}
+
+// Time-bounded wait on an mbarrier phase; also gives up when *abort becomes
+// nonzero (a shared flag another warp sets).  Returns false when it gave up.
+__device__ __forceinline__ bool MbarWaitFor(uint64_t* bar, uint32_t parity, uint64_t timeout_ns,
+                                            const volatile int* abort) {
+    const uint32_t addr = SmemAddr(bar);
+    const uint64_t t0 = GlobalTimerNs();
+    for (uint32_t spin = 0;; ++spin) {
+        uint32_t done;
+        asm volatile(
+            "{\n .reg .pred p;\n mbarrier.try_wait.parity.shared::cta.b64 p, [%1], %2;\n"
+            " selp.u32 %0, 1, 0, p;\n}\n"
+            : "=r"(done)
+            : "r"(addr), "r"(parity)
+            : "memory");
+        if (done) return true;
+        if ((spin & 63) == 63) {
+            if (abort && *abort) return false;
+            if (GlobalTimerNs() - t0 > timeout_ns) return false;
+        }
+    }
+}
+
 // Global -> shared bulk copy of `bytes` (multiple of 16, both addresses
 // 16-byte aligned), completing on `bar`.
 __device__ __forceinline__ void BulkLoad(void* smem_dst, const void* gmem_src, uint32_t bytes,

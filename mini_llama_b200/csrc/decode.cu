@@ -12,6 +12,11 @@
 // then RMSNorm -> lm_head GEMV -> arg-max (token and position stay on the
 // device).  Kernels are launched with programmatic dependent launch, so each
 // one streams its weights into shared memory while the previous one finishes.
+//
+// Q8_0 models whose shapes fit run instead the persistent decode kernel of
+// megakernel.cu: every step of a whole generate / decode call in one
+// cooperative launch.  The graph stays captured and can be selected with
+// mlb_session_use_persistent(session, 0).
 #include <algorithm>
 #include <array>
 #include <climits>
@@ -20,6 +25,7 @@
 #include <vector>
 
 #include "attention.cuh"
+#include "megakernel.cuh"
 #include "qgemv.cuh"
 #include "qmma.cuh"
 
@@ -71,6 +77,11 @@ struct mlb_model {
     size_t r16_bytes = 0;
     Slot r16_lm_head;
     std::vector<std::array<Slot, 15>> r16_layer;
+    // wo and w_down also in R16C (block columns contiguous) when the
+    // persistent decode kernel can run the model
+    bool r16c = false;
+    std::string mega_reason = "weights are not Q8_0";  // why not, when r16c is false
+    std::vector<std::array<Slot, 2>> r16c_layer;
 
     void* Ptr(const Slot& s) const { return s.bytes ? static_cast<char*>(arena) + s.offset : nullptr; }
     const Slot& Get(int l, int kind) const {
@@ -79,6 +90,9 @@ struct mlb_model {
     const uint8_t* R16(int l, int kind) const {
         const Slot& s = kind == MLB_W_LM_HEAD ? r16_lm_head : r16_layer[l][kind];
         return static_cast<const uint8_t*>(r16) + s.offset;
+    }
+    const uint8_t* R16C(int l, int kind) const {
+        return static_cast<const uint8_t*>(r16) + r16c_layer[l][kind == MLB_W_WO ? 0 : 1].offset;
     }
 };
 
@@ -101,6 +115,14 @@ struct mlb_session {
     int* hist = nullptr;   // [max_seq_len + 1]
     int chunks = 1;
     size_t cache_floats = 0;
+    // persistent decode kernel
+    bool mega_ok = false;  // the model's shapes fit it
+    std::string mega_reason;
+    bool mega = false;     // selected for generate / decode_device / forward
+    mlb::MegaParams mp = {};
+    size_t mega_smem = 0;
+    unsigned* counters = nullptr;
+    size_t counter_bytes = 0;
     cudaGraph_t graph = nullptr;
     cudaGraphExec_t exec = nullptr;
     std::vector<void*> allocations;
@@ -177,6 +199,34 @@ void RepackOne(mlb_model* m, DeviceContext& c, int l, int kind) {
     LinearShape(m->cfg, kind, rows, cols);
     const auto& src = m->Get(l, kind);
     LaunchRepackQ80R16(c, m->Ptr(src), rows, cols, const_cast<uint8_t*>(m->R16(l, kind)));
+    if (m->r16c && (kind == MLB_W_WO || kind == MLB_W_DOWN))
+        LaunchRepackQ80R16(c, m->Ptr(src), rows, cols, const_cast<uint8_t*>(m->R16C(l, kind)), true);
+}
+
+// Shapes the persistent decode kernel handles: whole 32-blocks everywhere,
+// head_dim 32, 64 or 128 (a K/V row is 8, 16 or 32 float4 lanes), and its
+// six-stage ring of the largest
+// item (two row tiles of a dim-wide weight, or one dim-tall block column)
+// plus its vectors within the shared-memory limit.
+// Empty when it fits, else the reason.
+std::string MegaShapeOk(const mlb_model_config& cf, const DeviceContext& c, int& stage_bytes) {
+    if (cf.weight_type != MLB_Q8_0) return "weights are not Q8_0";
+    if (cf.dim % 32 || cf.hidden_dim % 32) return "dim and hidden_dim must be multiples of 32";
+    if (cf.head_dim != 32 && cf.head_dim != 64 && cf.head_dim != 128)
+        return "head_dim must be 32, 64 or 128";
+    const int tile_b = (cf.dim / 32) * kR16Chunk;
+    const int col_b = ((cf.dim + 15) / 16) * kR16Chunk;
+    stage_bytes = std::max(2 * tile_b, col_b);
+    MegaParams p = {};
+    p.dim = cf.dim;
+    p.stage_bytes = stage_bytes;
+    int coop = 0;
+    cudaDeviceGetAttribute(&coop, cudaDevAttrCooperativeLaunch, c.device);
+    if (!coop) return "the device has no cooperative launch";
+    if (MegaSmemBytes(p) > static_cast<size_t>(c.max_smem_optin))
+        return "needs " + std::to_string(MegaSmemBytes(p)) + " B of shared memory, the device has " +
+               std::to_string(c.max_smem_optin);
+    return "";
 }
 
 // Q8_0 models keep an R16 copy of every linear weight for the integer-MMA GEMV.
@@ -207,6 +257,16 @@ void PrepareR16(mlb_model* m, DeviceContext& c, int chunks) {
     const int kinds[] = {MLB_W_WQ, MLB_W_WK, MLB_W_WV, MLB_W_WO, MLB_W_GATE, MLB_W_UP, MLB_W_DOWN};
     for (int l = 0; l < m->cfg.n_layers; ++l)
         for (int k : kinds) m->r16_layer[l][k] = slot(k);
+    int stage_bytes = 0;
+    m->mega_reason = MegaShapeOk(cf, c, stage_bytes);
+    m->r16c = m->mega_reason.empty();
+    if (m->r16c) {
+        m->r16c_layer.resize(m->cfg.n_layers);
+        for (int l = 0; l < m->cfg.n_layers; ++l) {
+            m->r16c_layer[l][0] = slot(MLB_W_WO);
+            m->r16c_layer[l][1] = slot(MLB_W_DOWN);
+        }
+    }
     m->r16_bytes = off;
     CheckCuda(cudaMallocAsync(&m->r16, off, c.stream), "cudaMallocAsync(R16 weights)");
     RepackOne(m, c, -1, MLB_W_LM_HEAD);
@@ -376,6 +436,95 @@ void CaptureStep(mlb_session* s, DeviceContext& c) {
     CheckCuda(cudaGraphInstantiate(&s->exec, s->graph, 0), "cudaGraphInstantiate");
 }
 
+// Sets up the persistent decode kernel for a session (when the model has its
+// R16C weights): the per-layer weight table on the device, a second
+// activation buffer, the phase counters and the launch parameters.
+void PrepareMega(mlb_session* s, DeviceContext& c) {
+    mlb_model* m = s->model;
+    if (!m->r16 || !m->r16c) {
+        s->mega_reason = m->r16 ? m->mega_reason : "no R16 weights (Q8_0 models only)";
+        return;
+    }
+    const mlb_model_config& cf = m->cfg;
+    int stage_bytes = 0;
+    s->mega_reason = MegaShapeOk(cf, c, stage_bytes);
+    if (!s->mega_reason.empty()) return;
+    std::vector<MegaLayer> layers(cf.n_layers);
+    for (int l = 0; l < cf.n_layers; ++l) {
+        auto F = [&](int kind) { return static_cast<const float*>(m->Ptr(m->Get(l, kind))); };
+        MegaLayer& L = layers[l];
+        L.wqkv[0] = m->R16(l, MLB_W_WQ);
+        L.wqkv[1] = m->R16(l, MLB_W_WK);
+        L.wqkv[2] = m->R16(l, MLB_W_WV);
+        L.bias[0] = F(MLB_W_BQ);
+        L.bias[1] = F(MLB_W_BK);
+        L.bias[2] = F(MLB_W_BV);
+        L.attn_norm = F(MLB_W_ATTN_NORM);
+        L.ffn_norm = F(MLB_W_FFN_NORM);
+        L.wo = m->R16C(l, MLB_W_WO);
+        L.gate = m->R16(l, MLB_W_GATE);
+        L.up = m->R16(l, MLB_W_UP);
+        L.down = m->R16C(l, MLB_W_DOWN);
+    }
+    MegaLayer* dl = static_cast<MegaLayer*>(DevAlloc(s, c, layers.size() * sizeof(MegaLayer)));
+    CheckCuda(cudaMemcpyAsync(dl, layers.data(), layers.size() * sizeof(MegaLayer),
+                              cudaMemcpyHostToDevice, c.stream),
+              "cudaMemcpyAsync(layer table)");
+    s->counter_bytes = size_t(3 * cf.n_layers + 2) * sizeof(unsigned);
+    s->counters = static_cast<unsigned*>(DevAlloc(s, c, s->counter_bytes));
+    float* x2 = static_cast<float*>(DevAlloc(s, c, size_t(cf.dim) * 4));
+    MegaParams& p = s->mp;
+    p.n_layers = cf.n_layers;
+    p.dim = cf.dim;
+    p.hidden = cf.hidden_dim;
+    p.vocab = cf.vocab_size;
+    p.n_heads = cf.n_heads;
+    p.n_kv = cf.n_kv_heads;
+    p.hd = cf.head_dim;
+    p.max_seq = cf.max_seq_len;
+    p.qd = cf.n_heads * cf.head_dim;
+    p.kd = cf.n_kv_heads * cf.head_dim;
+    p.group = cf.n_heads / cf.n_kv_heads;
+    p.eps = cf.rms_norm_eps;
+    p.scale = 1.0f / std::sqrt(static_cast<float>(cf.head_dim));
+    p.neox = cf.rope_type == MLB_ROPE_NEOX;
+    p.embedding = static_cast<const float*>(m->Ptr(m->global[MLB_W_EMBEDDING]));
+    p.final_norm = static_cast<const float*>(m->Ptr(m->global[MLB_W_FINAL_NORM]));
+    p.lm_head = m->R16(-1, MLB_W_LM_HEAD);
+    p.layers = dl;
+    p.rope_cos = m->rope_cos;
+    p.rope_sin = m->rope_sin;
+    p.kc = s->kc;
+    p.vc = s->vc;
+    p.xbuf[0] = s->x;
+    p.xbuf[1] = x2;
+    p.xmid = s->xmid;
+    p.qkv = s->qkv;
+    p.logits = s->logits;
+    p.am_val = s->am_val;
+    p.am_idx = s->am_idx;
+    p.counters = s->counters;
+    p.hist = s->hist;
+    p.next_token = s->state + 2;
+    p.status = s->state + 3;
+    p.stage_bytes = stage_bytes;
+    s->mega_smem = MegaSmemBytes(p);
+    s->mega_reason = MegaFits(p, s->mega_smem, c.sm_count);
+    s->mega_ok = s->mega_reason.empty();
+    s->mega = s->mega_ok;
+}
+
+// n_steps decode steps from start_pos in one launch of the persistent kernel;
+// hist[pos + 1] receives the arg-max when pos + 1 >= gen_from.
+void RunMega(mlb_session* s, DeviceContext& c, int start_pos, int n_steps, int gen_from) {
+    CheckCuda(cudaMemsetAsync(s->counters, 0, s->counter_bytes, c.stream), "cudaMemsetAsync(counters)");
+    MegaParams p = s->mp;
+    p.start_pos = start_pos;
+    p.n_steps = n_steps;
+    p.gen_from = gen_from;
+    LaunchMegaDecode(p, c.sm_count, s->mega_smem, c.stream);
+}
+
 void CheckStatus(mlb_session* s, DeviceContext& c) {
     int status = 0;
     CheckCuda(cudaMemcpyAsync(&status, s->state + 3, sizeof(int), cudaMemcpyDeviceToHost, c.stream),
@@ -540,6 +689,7 @@ int mlb_session_create(mlb_model* model, mlb_session** session) {
         CheckCuda(cudaMemsetAsync(s->hist, 0, size_t(cf.max_seq_len + 1) * 4, c.stream),
                   "cudaMemsetAsync");
         PrepareR16(model, c, s->chunks);
+        PrepareMega(s.get(), c);
         CheckCuda(cudaStreamSynchronize(c.stream), "cudaStreamSynchronize");
         CaptureStep(s.get(), c);
         *session = s.release();
@@ -586,7 +736,8 @@ int mlb_session_forward(mlb_session* session, int token, int pos, float* logits,
         CheckCuda(cudaMemcpyAsync(session->hist + pos, h + 2, sizeof(int), cudaMemcpyHostToDevice,
                                   c.stream),
                   "cudaMemcpyAsync(token)");
-        CheckCuda(cudaGraphLaunch(session->exec, c.stream), "cudaGraphLaunch");
+        if (session->mega) RunMega(session, c, pos, 1, INT_MAX);
+        else CheckCuda(cudaGraphLaunch(session->exec, c.stream), "cudaGraphLaunch");
         if (logits)
             CheckCuda(cudaMemcpyAsync(logits, session->logits, size_t(cf.vocab_size) * 4,
                                       cudaMemcpyDeviceToHost, c.stream),
@@ -618,8 +769,12 @@ int mlb_session_generate(mlb_session* session, const int* prompt, int n_prompt, 
                   "cudaMemcpyAsync(prompt)");
         SetState(session, c, start_pos, start_pos + n_prompt);
         const int steps = n_prompt + n_new - 1;
-        for (int i = 0; i < steps; ++i)
-            CheckCuda(cudaGraphLaunch(session->exec, c.stream), "cudaGraphLaunch");
+        if (session->mega) {
+            RunMega(session, c, start_pos, steps, start_pos + n_prompt);
+        } else {
+            for (int i = 0; i < steps; ++i)
+                CheckCuda(cudaGraphLaunch(session->exec, c.stream), "cudaGraphLaunch");
+        }
         CheckCuda(cudaMemcpyAsync(out_tokens, session->hist + start_pos + n_prompt, size_t(n_new) * 4,
                                   cudaMemcpyDeviceToHost, c.stream),
                   "cudaMemcpyAsync(tokens)");
@@ -640,8 +795,12 @@ int mlb_session_decode_device(mlb_session* session, int* tokens, int start_pos, 
                                   cudaMemcpyDeviceToDevice, c.stream),
                   "cudaMemcpyAsync(token)");
         SetState(session, c, start_pos, start_pos + 1);
-        for (int i = 0; i < n_steps; ++i)
-            CheckCuda(cudaGraphLaunch(session->exec, c.stream), "cudaGraphLaunch");
+        if (session->mega) {
+            RunMega(session, c, start_pos, n_steps, start_pos + 1);
+        } else {
+            for (int i = 0; i < n_steps; ++i)
+                CheckCuda(cudaGraphLaunch(session->exec, c.stream), "cudaGraphLaunch");
+        }
         CheckCuda(cudaMemcpyAsync(tokens + 1, session->hist + start_pos + 1, size_t(n_steps) * 4,
                                   cudaMemcpyDeviceToDevice, c.stream),
                   "cudaMemcpyAsync(tokens)");
@@ -658,7 +817,28 @@ int mlb_session_logits(mlb_session* session, const float** logits) {
 int mlb_session_gemv_path(mlb_session* session, int* path) {
     return Guard([&] {
         Require(session && path, "mlb_session_gemv_path", "null argument");
-        *path = session->model->r16 ? 1 : 0;
+        *path = session->mega ? 2 : (session->model->r16 ? 1 : 0);
+    });
+}
+
+int mlb_session_trace(mlb_session* session, unsigned long long* device_buffer, size_t entries) {
+    return Guard([&] {
+        Require(session != nullptr, "mlb_session_trace", "null session");
+        Require(device_buffer != nullptr || entries == 0, "mlb_session_trace", "null buffer");
+        session->mp.trace = device_buffer;
+        session->mp.trace_cap = device_buffer ? entries : 0;
+    });
+}
+
+int mlb_session_use_persistent(mlb_session* session, int enable) {
+    return Guard([&] {
+        Require(session != nullptr, "mlb_session_use_persistent", "null session");
+        Require(!enable || session->mega_ok, "mlb_session_use_persistent",
+                "the persistent decode kernel does not support this model: " + session->mega_reason,
+                MLB_ERR_UNSUPPORTED);
+        DeviceContext& c = Ctx(session->model->device);
+        CheckCuda(cudaStreamSynchronize(c.stream), "cudaStreamSynchronize");
+        session->mega = enable != 0;
     });
 }
 

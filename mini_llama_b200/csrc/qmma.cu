@@ -82,11 +82,13 @@ void LaunchQmmaStore(const GemvParams& p, const GemvPlan& plan, cudaStream_t str
     Fail(MLB_ERR_UNSUPPORTED, "integer-MMA GEMV: unsupported row count");
 }
 
-void LaunchRepackQ80R16(DeviceContext& c, const void* src, int rows, int cols, void* dst) {
+void LaunchRepackQ80R16(DeviceContext& c, const void* src, int rows, int cols, void* dst,
+                        bool column_major) {
     const long long items = (rows + 15) / 16 * 16LL * ((cols + 31) / 32);
     const long long blocks = std::min<long long>((items + 255) / 256, 8LL * c.sm_count);
     RepackQ80R16Kernel<<<static_cast<unsigned>(std::max<long long>(blocks, 1)), 256, 0, c.stream>>>(
-        static_cast<const uint8_t*>(src), rows, cols, static_cast<uint8_t*>(dst));
+        static_cast<const uint8_t*>(src), rows, cols, static_cast<uint8_t*>(dst),
+        column_major ? 1 : 0);
     CheckCuda(cudaGetLastError(), "RepackQ80R16Kernel");
 }
 

@@ -34,7 +34,11 @@ __host__ __device__ inline size_t R16Bytes(int rows, int cols) {
 }
 
 // GGUF Q8_0 [N, nb] -> R16.  One thread per (row, block) of the padded rows.
-static __global__ void RepackQ80R16Kernel(const uint8_t* src, int rows, int cols, uint8_t* dst) {
+// column_major = 1 orders the chunks by block column instead ("R16C": chunk
+// (t, b) at b * ntiles + t), so one block column of every row tile -- the
+// weights a split-K partial over 32 inputs needs -- is contiguous.
+static __global__ void RepackQ80R16Kernel(const uint8_t* src, int rows, int cols, uint8_t* dst,
+                                          int column_major) {
     const int nb = (cols + 31) / 32;
     const long long prow = (rows + 15) / 16 * 16LL;
     const long long total = prow * nb;
@@ -42,7 +46,8 @@ static __global__ void RepackQ80R16Kernel(const uint8_t* src, int rows, int cols
          idx += 1LL * gridDim.x * blockDim.x) {
         const int r = static_cast<int>(idx / nb), b = static_cast<int>(idx % nb);
         const int t = r >> 4, i = r & 15;
-        uint8_t* chunk = dst + (size_t(t) * nb + b) * kR16Chunk;
+        const size_t ntiles = static_cast<size_t>((rows + 15) / 16);
+        uint8_t* chunk = dst + (column_major ? size_t(b) * ntiles + t : size_t(t) * nb + b) * kR16Chunk;
         uint8_t q[32];
         uint16_t d = 0;
         if (r < rows) {
@@ -347,6 +352,7 @@ GemvPlan PlanQmma(GemvParams& p, int M, bool dual, int sm_count, int max_smem, i
 void LaunchQmmaDecode(int pro, int epi, const GemvParams& p, const GemvPlan& plan,
                       cudaStream_t stream);
 void LaunchQmmaStore(const GemvParams& p, const GemvPlan& plan, cudaStream_t stream);
-void LaunchRepackQ80R16(DeviceContext& c, const void* src, int rows, int cols, void* dst);
+void LaunchRepackQ80R16(DeviceContext& c, const void* src, int rows, int cols, void* dst,
+                        bool column_major = false);
 
 }  // namespace mlb

@@ -175,6 +175,15 @@ class Session:
     def decode_device(self, tokens_ptr: int, start_pos: int, n_steps: int):
         self.lib.call("mlb_session_decode_device", self.handle, tokens_ptr, start_pos, n_steps)
 
+    def path(self) -> int:
+        """2 persistent kernel, 1 graph with integer-MMA GEMV, 0 graph with SIMT GEMV."""
+        v = ctypes.c_int(-1)
+        self.lib.call("mlb_session_gemv_path", self.handle, ctypes.byref(v))
+        return v.value
+
+    def use_persistent(self, enable: bool):
+        self.lib.call("mlb_session_use_persistent", self.handle, 1 if enable else 0)
+
     def logits_ptr(self) -> int:
         p = ctypes.c_void_p()
         self.lib.call("mlb_session_logits", self.handle, ctypes.byref(p))

@@ -1,6 +1,8 @@
-"""Whole-model parity of the decode session (one CUDA graph per token) against
-the reference CPU path: greedy tokens bit-exact, logits within 1e-3 relative
-(|a - e| <= 1e-3 * max(1, max|e|) over the vocabulary)."""
+"""Whole-model parity of the decode session against the reference CPU path:
+greedy tokens bit-exact, logits within 1e-3 relative (|a - e| <= 1e-3 *
+max(1, max|e|) over the vocabulary).  The Qwen2 cases run through both decode
+paths of a Q8_0 session: the persistent decode kernel (path 2) and the CUDA
+graph per token (path 1)."""
 import numpy as np
 import pytest
 
@@ -73,6 +75,16 @@ def qwen2(mlb, gpu):
     m.close()
 
 
+@pytest.fixture(params=[2, 1], ids=["persistent", "graph"])
+def qwen2_session(request, qwen2):
+    s = Session(qwen2)
+    if request.param == 1:
+        s.use_persistent(False)
+    assert s.path() == request.param
+    yield s
+    s.close()
+
+
 def test_qwen2_device_weights_equal_oracle(mlb, gpu, oracle, qwen2):
     """Weights generated and quantized on the device equal the oracle's."""
     from oracle import binding as ob
@@ -92,57 +104,51 @@ def test_qwen2_device_weights_equal_oracle(mlb, gpu, oracle, qwen2):
     assert np.array_equal(got, oracle.normal(128, 3, ob.stream_layer(5, 8), 0.02))
 
 
-def test_qwen2_greedy_128_tokens_bit_exact(mlb, gpu, qwen2, golden_qwen2):
-    s = Session(qwen2)
-    try:
-        prompt = golden_qwen2["model_qwen2_prompt"]
-        gen = golden_qwen2["model_qwen2_generated"]
-        out = s.generate(prompt, len(gen))
-        mismatch = np.flatnonzero(out != gen)
-        assert mismatch.size == 0, f"first mismatch at generated token {mismatch[:3]}"
-    finally:
-        s.close()
+def test_qwen2_greedy_128_tokens_bit_exact(mlb, gpu, qwen2_session, golden_qwen2):
+    s = qwen2_session
+    prompt = golden_qwen2["model_qwen2_prompt"]
+    gen = golden_qwen2["model_qwen2_generated"]
+    out = s.generate(prompt, len(gen))
+    mismatch = np.flatnonzero(out != gen)
+    assert mismatch.size == 0, f"first mismatch at generated token {mismatch[:3]}"
+    # a second call on the same session (fresh counters, same cache layout)
+    s.reset()
+    assert np.array_equal(s.generate(prompt, 16), gen[:16])
 
 
-def test_qwen2_logits_per_step(mlb, gpu, qwen2, golden_qwen2):
+def test_qwen2_logits_per_step(mlb, gpu, qwen2_session, golden_qwen2):
     """Per-step top-8 logits of the reference CPU path, and the full logits of
     the last prompt position, through single-token forwards."""
-    s = Session(qwen2)
-    try:
-        prompt = list(golden_qwen2["model_qwen2_prompt"])
-        gen = list(golden_qwen2["model_qwen2_generated"])
-        tokens = prompt + gen
-        top_idx = golden_qwen2["model_qwen2_top_idx"].reshape(-1, 8)
-        top_val = golden_qwen2["model_qwen2_top_val"].reshape(-1, 8)
-        scale = max(1.0, float(np.abs(top_val).max()))
-        for step in range(len(tokens) - 1):
-            logits, nxt = s.forward(tokens[step], step)
-            err = float(np.abs(logits[top_idx[step]] - top_val[step]).max())
-            assert err <= LOGIT_TOL * scale, f"step {step}: top-8 error {err:.3e}"
-            if step == len(prompt) - 1:
-                assert_logits(logits, golden_qwen2["model_qwen2_logits"], "last prompt step")
-            if step >= len(prompt) - 1:
-                assert nxt == tokens[step + 1], f"token at step {step}"
-    finally:
-        s.close()
+    s = qwen2_session
+    prompt = list(golden_qwen2["model_qwen2_prompt"])
+    gen = list(golden_qwen2["model_qwen2_generated"])
+    tokens = prompt + gen
+    top_idx = golden_qwen2["model_qwen2_top_idx"].reshape(-1, 8)
+    top_val = golden_qwen2["model_qwen2_top_val"].reshape(-1, 8)
+    scale = max(1.0, float(np.abs(top_val).max()))
+    for step in range(len(tokens) - 1):
+        logits, nxt = s.forward(tokens[step], step)
+        err = float(np.abs(logits[top_idx[step]] - top_val[step]).max())
+        assert err <= LOGIT_TOL * scale, f"step {step}: top-8 error {err:.3e}"
+        if step == len(prompt) - 1:
+            assert_logits(logits, golden_qwen2["model_qwen2_logits"], "last prompt step")
+        if step >= len(prompt) - 1:
+            assert nxt == tokens[step + 1], f"token at step {step}"
 
 
-def test_session_device_decode_matches_generate(mlb, gpu, qwen2, golden_qwen2):
+def test_session_device_decode_matches_generate(mlb, gpu, qwen2_session, golden_qwen2):
     """The measurement entry point (tokens on the device) produces the same
     greedy continuation as mlb_session_generate."""
-    s = Session(qwen2)
-    try:
-        prompt = golden_qwen2["model_qwen2_prompt"]
-        gen = golden_qwen2["model_qwen2_generated"]
-        s.generate(prompt, 1)  # prefill positions 0..63, first token at 64
-        toks = DeviceArray(mlb, gpu, 128, np.int32)
-        first = np.zeros(128, np.int32)
-        first[0] = gen[0]
-        toks.upload(first)
-        s.decode_device(toks.ptr, len(prompt), 127)
-        assert np.array_equal(toks.download()[1:], gen[1:128])
-    finally:
-        s.close()
+    s = qwen2_session
+    prompt = golden_qwen2["model_qwen2_prompt"]
+    gen = golden_qwen2["model_qwen2_generated"]
+    s.generate(prompt, 1)  # prefill positions 0..63, first token at 64
+    toks = DeviceArray(mlb, gpu, 128, np.int32)
+    first = np.zeros(128, np.int32)
+    first[0] = gen[0]
+    toks.upload(first)
+    s.decode_device(toks.ptr, len(prompt), 127)
+    assert np.array_equal(toks.download()[1:], gen[1:128])
 
 
 def test_session_rejects_bad_inputs(mlb, gpu, qwen2):
@@ -163,12 +169,17 @@ def test_session_rejects_bad_inputs(mlb, gpu, qwen2):
 
 
 def test_q8_0_session_uses_integer_mma_path(mlb, gpu, qwen2):
-    """A Q8_0 model decodes through the integer-MMA GEMV over R16 weights."""
+    """A Q8_0 model decodes through the persistent kernel by default; the
+    graph of integer-MMA GEMVs over R16 weights stays selectable."""
     import ctypes
     s = Session(qwen2)
     try:
         path = ctypes.c_int(-1)
         mlb.call("mlb_session_gemv_path", s.handle, ctypes.byref(path))
-        assert path.value == 1
+        assert path.value == 2
+        s.use_persistent(False)
+        assert s.path() == 1
+        s.use_persistent(True)
+        assert s.path() == 2
     finally:
         s.close()
