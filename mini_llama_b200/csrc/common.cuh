@@ -197,6 +197,23 @@ __device__ __forceinline__ void BulkLoad(void* smem_dst, const void* gmem_src, u
         : "memory");
 }
 
+// L2 policy for data read once per pass (streamed weights): evicted first, so
+// it does not push out what is reused (KV cache, activations, counters).
+__device__ __forceinline__ uint64_t L2EvictFirstPolicy() {
+    uint64_t pol;
+    asm volatile("createpolicy.fractional.L2::evict_first.b64 %0, 1.0;" : "=l"(pol));
+    return pol;
+}
+
+// BulkLoad with an L2 cache policy (L2EvictFirstPolicy).
+__device__ __forceinline__ void BulkLoadHint(void* smem_dst, const void* gmem_src, uint32_t bytes,
+                                             uint64_t* bar, uint64_t policy) {
+    asm volatile(
+        "cp.async.bulk.shared::cluster.global.mbarrier::complete_tx::bytes.L2::cache_hint [%0], [%1], %2, [%3], %4;"
+        ::"r"(SmemAddr(smem_dst)), "l"(gmem_src), "r"(bytes), "r"(SmemAddr(bar)), "l"(policy)
+        : "memory");
+}
+
 // Asynchronous global -> shared copies (cp.async): every copy of a batch is in
 // flight at once, so staging a vector costs one memory round trip.
 __device__ __forceinline__ void CpAsync4(void* smem_dst, const void* gmem_src) {

@@ -77,8 +77,8 @@ struct mlb_model {
     size_t r16_bytes = 0;
     Slot r16_lm_head;
     std::vector<std::array<Slot, 15>> r16_layer;
-    // wo and w_down also in R16C (block columns contiguous) when the
-    // persistent decode kernel can run the model
+    // wo also in R16C (block columns contiguous) when the persistent decode
+    // kernel can run the model
     bool r16c = false;
     std::string mega_reason = "weights are not Q8_0";  // why not, when r16c is false
     std::vector<std::array<Slot, 2>> r16c_layer;
@@ -92,7 +92,7 @@ struct mlb_model {
         return static_cast<const uint8_t*>(r16) + s.offset;
     }
     const uint8_t* R16C(int l, int kind) const {
-        return static_cast<const uint8_t*>(r16) + r16c_layer[l][kind == MLB_W_WO ? 0 : 1].offset;
+        return static_cast<const uint8_t*>(r16) + r16c_layer[l][0].offset;
     }
 };
 
@@ -199,7 +199,7 @@ void RepackOne(mlb_model* m, DeviceContext& c, int l, int kind) {
     LinearShape(m->cfg, kind, rows, cols);
     const auto& src = m->Get(l, kind);
     LaunchRepackQ80R16(c, m->Ptr(src), rows, cols, const_cast<uint8_t*>(m->R16(l, kind)));
-    if (m->r16c && (kind == MLB_W_WO || kind == MLB_W_DOWN))
+    if (m->r16c && kind == MLB_W_WO)
         LaunchRepackQ80R16(c, m->Ptr(src), rows, cols, const_cast<uint8_t*>(m->R16C(l, kind)), true);
 }
 
@@ -218,8 +218,16 @@ std::string MegaShapeOk(const mlb_model_config& cf, const DeviceContext& c, int&
     const int col_b = ((cf.dim + 15) / 16) * kR16Chunk;
     stage_bytes = std::max(2 * tile_b, col_b);
     MegaParams p = {};
+    p.n_layers = cf.n_layers;
     p.dim = cf.dim;
+    p.hidden = cf.hidden_dim;
+    p.vocab = cf.vocab_size;
+    p.n_heads = cf.n_heads;
+    p.hd = cf.head_dim;
+    p.qd = cf.n_heads * cf.head_dim;
+    p.kd = cf.n_kv_heads * cf.head_dim;
     p.stage_bytes = stage_bytes;
+    p.list_cap = MegaListCap(p, c.sm_count);
     int coop = 0;
     cudaDeviceGetAttribute(&coop, cudaDevAttrCooperativeLaunch, c.device);
     if (!coop) return "the device has no cooperative launch";
@@ -262,10 +270,7 @@ void PrepareR16(mlb_model* m, DeviceContext& c, int chunks) {
     m->r16c = m->mega_reason.empty();
     if (m->r16c) {
         m->r16c_layer.resize(m->cfg.n_layers);
-        for (int l = 0; l < m->cfg.n_layers; ++l) {
-            m->r16c_layer[l][0] = slot(MLB_W_WO);
-            m->r16c_layer[l][1] = slot(MLB_W_DOWN);
-        }
+        for (int l = 0; l < m->cfg.n_layers; ++l) m->r16c_layer[l][0] = slot(MLB_W_WO);
     }
     m->r16_bytes = off;
     CheckCuda(cudaMallocAsync(&m->r16, off, c.stream), "cudaMallocAsync(R16 weights)");
@@ -464,13 +469,13 @@ void PrepareMega(mlb_session* s, DeviceContext& c) {
         L.wo = m->R16C(l, MLB_W_WO);
         L.gate = m->R16(l, MLB_W_GATE);
         L.up = m->R16(l, MLB_W_UP);
-        L.down = m->R16C(l, MLB_W_DOWN);
+        L.down = m->R16(l, MLB_W_DOWN);
     }
     MegaLayer* dl = static_cast<MegaLayer*>(DevAlloc(s, c, layers.size() * sizeof(MegaLayer)));
     CheckCuda(cudaMemcpyAsync(dl, layers.data(), layers.size() * sizeof(MegaLayer),
                               cudaMemcpyHostToDevice, c.stream),
               "cudaMemcpyAsync(layer table)");
-    s->counter_bytes = size_t(3 * cf.n_layers + 2) * sizeof(unsigned);
+    s->counter_bytes = size_t(kMkPhases * cf.n_layers + 2) * sizeof(unsigned);
     s->counters = static_cast<unsigned*>(DevAlloc(s, c, s->counter_bytes));
     float* x2 = static_cast<float*>(DevAlloc(s, c, size_t(cf.dim) * 4));
     MegaParams& p = s->mp;
@@ -500,6 +505,7 @@ void PrepareMega(mlb_session* s, DeviceContext& c) {
     p.xbuf[1] = x2;
     p.xmid = s->xmid;
     p.qkv = s->qkv;
+    p.ff = s->ff;
     p.logits = s->logits;
     p.am_val = s->am_val;
     p.am_idx = s->am_idx;
@@ -508,6 +514,7 @@ void PrepareMega(mlb_session* s, DeviceContext& c) {
     p.next_token = s->state + 2;
     p.status = s->state + 3;
     p.stage_bytes = stage_bytes;
+    p.list_cap = MegaListCap(p, c.sm_count);
     s->mega_smem = MegaSmemBytes(p);
     s->mega_reason = MegaFits(p, s->mega_smem, c.sm_count);
     s->mega_ok = s->mega_reason.empty();
@@ -534,7 +541,9 @@ void CheckStatus(mlb_session* s, DeviceContext& c) {
         CheckCuda(cudaMemsetAsync(s->state + 3, 0, sizeof(int), c.stream), "cudaMemsetAsync");
         Fail(status, status == MLB_ERR_DEVICE_TIMEOUT
                          ? "mlb_session: a bounded device wait expired"
-                         : "mlb_session: token id out of range on the device");
+                         : status == MLB_ERR_UNSUPPORTED
+                               ? "mlb_session: persistent kernel schedule exceeds its list"
+                               : "mlb_session: token id out of range on the device");
     }
 }
 

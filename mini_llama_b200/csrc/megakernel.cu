@@ -29,10 +29,32 @@ __device__ __forceinline__ void RedAdd(float* p, float v) {
     asm volatile("red.global.add.f32 [%0], %1;" ::"l"(p), "f"(v) : "memory");
 }
 
+__host__ __device__ constexpr size_t Round128(size_t b) { return (b + 127) & ~size_t(127); }
+
+struct Chunk {  // one ring stage of the schedule: one or two bulk copies, back to back
+    const uint8_t* src;
+    const uint8_t* src2;  // null, or the second copy (placed at bytes)
+    uint32_t bytes;
+    uint32_t bytes2;
+};
+
+// Shared-memory layout: fixed-size buffers at constant offsets, then
+// xs, nw [dim], the digit planes and block scales of xs, then the ring.
+constexpr size_t kOffFull = 0;                                            // kMkStages mbarriers
+constexpr size_t kOffFlags = kOffFull + Round128(8 * kMkStages);          // 8 ints
+constexpr size_t kOffScratch = kOffFlags + 128;                           // 32 floats
+constexpr size_t kOffVsx = kOffScratch + 128;                             // 4 floats
+constexpr size_t kOffVdig = kOffVsx + 128;                                // 4 planes of 4 blocks
+constexpr size_t kOffRed = kOffVdig + Round128(4 * (4 * 32 + 16));        // 8 warps x 32
+constexpr size_t kOffVec = kOffRed + 4 * 8 * 32;                          // 512 floats
+constexpr size_t kOffAtt = kOffVec + 4 * 512;                             // 8 warps x 128
+constexpr size_t kOffSc = kOffAtt + 4 * 8 * 128;                          // kMkAttnChunk floats
+constexpr size_t kOffFixedEnd = kOffSc + Round128(4 * kMkAttnChunk);
+
 struct MkSmem {  // flags[0] is the CTA's abort flag (read by the producer warp too)
     uint8_t* ring;
     uint64_t* full;
-    uint64_t* empty;
+    struct Chunk* list;  // the CTA's chunk sequence of one step
     float* xs;      // [dim] activation (then normalised)
     float* nw;      // [dim] norm weights
     int8_t* dig;    // 4 digit planes of xs, stride DigitStride(nb_dim)
@@ -43,8 +65,12 @@ struct MkSmem {  // flags[0] is the CTA's abort flag (read by the producer warp 
     float* vec;     // [4 * 128] small vectors (g, u / q, k, v, o)
     float* att;     // [8 warps][hd] attention partials
     float* sc;      // [kMkAttnChunk] scores / weights of a chunk of positions
+    float* acc;     // [dim] block-column / down products of the CTA, flushed by red.add
+    float* fx;      // [hidden] the ff blocks FFN-B needs
+    int8_t* fdig;   // 4 digit planes of fx, stride DigitStride(hidden / 32)
+    float* fsx;     // [hidden / 32] their block scales
     float* scratch; // [32]
-    int* flags;     // [0] abort, [1] token
+    int* flags;     // [0] abort, [1] token, [2] chunks per step, [4] decision, [5] chunks issued
 };
 
 __device__ __forceinline__ int WorkerCount(int G, int T) { return T < G ? T : G; }
@@ -61,29 +87,46 @@ __device__ __forceinline__ void Trace(const MegaParams& p, int step, int l, int 
 // ---------------------------------------------------------------- waits
 // Consumer side: thread 0 polls the counter (acquire) until it reaches
 // `target`; everybody then learns whether to go on.  Returns false on abort.
-__device__ bool WaitCounter(const MegaParams& p, const MkSmem& s, int ctr, unsigned target) {
+// Ring state of the consumers (identical in every thread): chunk n is the
+// next to consume; chunk n + kMkStages, list entry li, is the next to issue.
+struct Ring {
+    unsigned n;
+    unsigned li;
+    unsigned len;    // chunks per step (list length)
+    unsigned total;  // chunks of the launch
+    uint64_t pol;    // L2 evict-first policy of the weight copies
+};
+
+// Uniform go / abort decision at a phase wait: thread 0 polls the counter
+// (acquire; bounded, and it gives up when the status word is set), writes the
+// decision between two barriers, and every thread reads it.  flags[0] is the
+// CTA's sticky abort flag (any thread may set it), flags[4] the decision.
+__device__ __forceinline__ bool WaitCounter(const MegaParams& p, const MkSmem& s, int ctr, unsigned target) {
+    ConsumerBar();
     if (threadIdx.x == 0) {
-        bool ok = false;
-        for (int it = 0; it < kMkSpin; ++it) {
-            if (LdAcquire(p.counters + ctr) >= target) {
-                ok = true;
-                break;
+        bool ok = s.flags[0] == 0;
+        if (ok) {
+            ok = false;
+            for (int it = 0; it < kMkSpin; ++it) {
+                if (LdAcquire(p.counters + ctr) >= target) {
+                    ok = true;
+                    break;
+                }
+                if ((it & 255) == 255 && LdRelaxedInt(p.status) != 0) break;
             }
-            if ((it & 255) == 255 && LdRelaxedInt(p.status) != 0) break;
+            if (!ok) atomicCAS(p.status, 0, MLB_ERR_DEVICE_TIMEOUT);
         }
-        if (!ok) {
-            atomicCAS(p.status, 0, MLB_ERR_DEVICE_TIMEOUT);
-            s.flags[0] = 1;
-        }
+        if (!ok) s.flags[0] = 1;
+        s.flags[4] = ok ? 1 : 0;
     }
     ConsumerBar();
-    return s.flags[0] == 0;
+    return s.flags[4] != 0;
 }
 
 // Publishes this CTA's writes of the phase and increments the counter: the
 // barrier orders every consumer thread's writes before thread 0's fence, which
 // is cumulative over them, then the increment.
-__device__ void Signal(const MegaParams& p, int ctr) {
+__device__ __forceinline__ void Signal(const MegaParams& p, int ctr) {
     ConsumerBar();
     if (threadIdx.x == 0) {
         __threadfence();
@@ -91,25 +134,42 @@ __device__ void Signal(const MegaParams& p, int ctr) {
     }
 }
 
-// Waits for the stage of chunk n (every consumer thread observes the phase),
-// bounded; the barrier after it makes the go/abort decision uniform.
-__device__ bool WaitChunk(const MegaParams& p, const MkSmem& s, unsigned n) {
-    const int slot = n % kMkStages;
-    const bool ok = MbarWaitFor(&s.full[slot], (n / kMkStages) & 1, kMkWaitNs, s.flags);
-    if (!ok) {
+// Waits (every thread) for the stage of chunk rg.n; bounded, and it gives up
+// as soon as the status word is set.  A wait that gives up records the error
+// and sets the sticky abort flag but returns normally: every thread still
+// reaches every barrier, and the CTA leaves at its next phase wait.
+__device__ __forceinline__ void WaitChunk(const MegaParams& p, const MkSmem& s, const Ring& rg) {
+    if (!MbarWaitFor(&s.full[rg.n % kMkStages], (rg.n / kMkStages) & 1, kMkWaitNs, p.status)) {
         atomicCAS(p.status, 0, MLB_ERR_DEVICE_TIMEOUT);
         s.flags[0] = 1;
     }
-    ConsumerBar();
-    return s.flags[0] == 0;
 }
 
-// After every consumer thread is done with chunk n's stage.
-__device__ void ReleaseChunk(const MkSmem& s, unsigned n) {
+__device__ __forceinline__ uint8_t* StagePtr(const MegaParams& p, const MkSmem& s, const Ring& rg) {
+    return s.ring + size_t(rg.n % kMkStages) * p.stage_bytes;
+}
+
+// List entry li into ring slot k % kMkStages; thread 0 only.
+__device__ __forceinline__ void IssueChunk(const MegaParams& p, const MkSmem& s, unsigned k, unsigned li,
+                                           uint64_t pol) {
+    const Chunk ch = s.list[li];
+    const int slot = k % kMkStages;
+    uint8_t* dst = s.ring + size_t(slot) * p.stage_bytes;
+    MbarExpectTx(&s.full[slot], ch.bytes + ch.bytes2);
+    BulkLoadHint(dst, ch.src, ch.bytes, &s.full[slot], pol);
+    if (ch.src2) BulkLoadHint(dst + ch.bytes, ch.src2, ch.bytes2, &s.full[slot], pol);
+    ++s.flags[5];  // chunks issued
+}
+
+// After every thread is done with chunk rg.n's stage (the barrier): the slot
+// takes chunk rg.n + kMkStages (unless the CTA is aborting), and the ring
+// moves on.
+__device__ __forceinline__ void ReleaseChunk(const MegaParams& p, const MkSmem& s, Ring& rg) {
     ConsumerBar();
-    if (threadIdx.x == 0)
-        asm volatile("mbarrier.arrive.shared::cta.b64 _, [%0];" ::"r"(SmemAddr(&s.empty[n % kMkStages]))
-                     : "memory");
+    const unsigned k = rg.n + kMkStages;
+    if (threadIdx.x == 0 && k < rg.total && s.flags[0] == 0) IssueChunk(p, s, k, rg.li, rg.pol);
+    ++rg.n;
+    rg.li = rg.li + 1 == rg.len ? 0 : rg.li + 1;
 }
 
 // ---------------------------------------------------------------- vectors
@@ -130,6 +190,57 @@ __device__ float ConsumerSum(float v, float* scratch) {
     return t;
 }
 
+// Round to nearest even for |v| < 2^22 (the digit scaling guarantees it):
+// adding 1.5 * 2^23 leaves the rounded integer in the low mantissa bits.
+__device__ __forceinline__ int RoundSmall(float v) {
+    return __float_as_int(v + 12582912.0f) - 0x4B400000;
+}
+
+// Digit planes and scales of the count blocks (start + i) mod nb of x (in
+// shared memory, block b at x + 32 b), stored at block b of dig / sx: eight
+// threads per block, four elements each (the block max by three shuffles).
+__device__ __forceinline__ void DigitsBlocks(const float* x, int start, int count, int nb, int8_t* dig,
+                                          int dstride, float* sx) {
+    for (int k0 = 0; k0 < count * 8; k0 += 256) {  // count * 8 threads, groups of 8 share a trip
+        const int k = k0 + threadIdx.x;
+        const bool on = k < count * 8;
+        const int b = on ? (start + k / 8) % nb : 0, e = 4 * (k % 8);
+        float4 v = make_float4(0.f, 0.f, 0.f, 0.f);
+        if (on) v = *reinterpret_cast<const float4*>(x + b * 32 + e);
+        float mx = fmaxf(fmaxf(fabsf(v.x), fabsf(v.y)), fmaxf(fabsf(v.z), fabsf(v.w)));
+        mx = fmaxf(mx, __shfl_xor_sync(0xffffffffu, mx, 1));
+        mx = fmaxf(mx, __shfl_xor_sync(0xffffffffu, mx, 2));
+        mx = fmaxf(mx, __shfl_xor_sync(0xffffffffu, mx, 4));
+        if (!on) continue;
+        const int ex = static_cast<int>((__float_as_uint(mx) >> 23) & 0xff) - 126;
+        const float y[4] = {v.x, v.y, v.z, v.w};
+        uint32_t p2 = 0, p1 = 0, p0 = 0;
+        float sc = 0.0f;
+        if (mx > 0.0f && ex >= -104) {
+            const float up = __uint_as_float(static_cast<uint32_t>(127 + 22 - ex) << 23);
+            sc = __uint_as_float(static_cast<uint32_t>(127 + ex - 22) << 23);
+#pragma unroll
+            for (int j = 0; j < 4; ++j) {
+                const int xi = RoundSmall(y[j] * up);
+                const int d0 = (xi << 24) >> 24;
+                const int x1 = (xi - d0) >> 8;
+                const int d1 = (x1 << 24) >> 24;
+                const int d2 = (x1 - d1) >> 8;
+                p2 |= (static_cast<uint32_t>(d2) & 0xffu) << (8 * j);
+                p1 |= (static_cast<uint32_t>(d1) & 0xffu) << (8 * j);
+                p0 |= (static_cast<uint32_t>(d0) & 0xffu) << (8 * j);
+            }
+        }
+        uint32_t* base = reinterpret_cast<uint32_t*>(dig + b * 32 + e);
+        base[0] = p2;
+        base[dstride / 4] = p1;
+        base[2 * (dstride / 4)] = p0;
+        base[3 * (dstride / 4)] = 0u;
+        if ((k & 7) == 0) sx[b] = sc;
+    }
+    ConsumerBar();
+}
+
 __device__ float ConsumerMax(float v, float* scratch) {
     v = WarpMax(v);
     const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
@@ -142,40 +253,66 @@ __device__ float ConsumerMax(float v, float* scratch) {
     return t;
 }
 
-// In place x = x * rsqrt(mean(x^2) + eps) * w (the reference's product order).
-__device__ void RmsNormSmem(float* x, const float* w, int n, float eps, float* scratch) {
+// RMSNorm of x (n % 32 == 0, in shared memory) straight into the digit planes
+// and block scales of the normalised vector, which is not stored: a thread
+// per four elements, eight threads per 32-block (the block max by three
+// shuffles).  Each normalised value is x * rsqrt(mean(x^2) + eps) * w in the
+// reference's product order.
+__device__ __forceinline__ void RmsNormDigits(const float* x, const float* w, int n, float eps, int8_t* dig,
+                              int dstride, float* sx, float* scratch) {
+    const int n4 = n / 4;
     float ss = 0.0f;
-    for (int i = threadIdx.x; i < n; i += 256) ss = fmaf(x[i], x[i], ss);
+    for (int i = threadIdx.x; i < n4; i += 256) {
+        const float4 v = reinterpret_cast<const float4*>(x)[i];
+        ss = fmaf(v.x, v.x, ss);
+        ss = fmaf(v.y, v.y, ss);
+        ss = fmaf(v.z, v.z, ss);
+        ss = fmaf(v.w, v.w, ss);
+    }
     const float tot = ConsumerSum(ss, scratch);
     const float scale = 1.0f / sqrtf(tot / static_cast<float>(n) + eps);
-    for (int i = threadIdx.x; i < n; i += 256) x[i] = x[i] * scale * w[i];
-    ConsumerBar();
-}
-
-// Digit planes (qmma.cuh) of nb blocks of x, one warp per block.
-__device__ void DigitsMk(const float* x, int nb, int8_t* dig, int dstride, float* sx) {
-    const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
-    for (int b = warp; b < nb; b += kMkConsumerWarps) {
-        const float v = x[b * 32 + lane];
-        const float mx = WarpMax(fabsf(v));
+    // n4 is a multiple of 8, so the eight threads of a block share every trip
+    for (int i0 = 0; i0 < n4; i0 += 256) {
+        const int i = i0 + threadIdx.x;
+        const bool on = i < n4;
+        float y[4] = {0.f, 0.f, 0.f, 0.f};
+        if (on) {
+            const float4 v = reinterpret_cast<const float4*>(x)[i];
+            const float4 g = reinterpret_cast<const float4*>(w)[i];
+            y[0] = v.x * scale * g.x;
+            y[1] = v.y * scale * g.y;
+            y[2] = v.z * scale * g.z;
+            y[3] = v.w * scale * g.w;
+        }
+        float mx = fmaxf(fmaxf(fabsf(y[0]), fabsf(y[1])), fmaxf(fabsf(y[2]), fabsf(y[3])));
+        mx = fmaxf(mx, __shfl_xor_sync(0xffffffffu, mx, 1));
+        mx = fmaxf(mx, __shfl_xor_sync(0xffffffffu, mx, 2));
+        mx = fmaxf(mx, __shfl_xor_sync(0xffffffffu, mx, 4));
+        if (!on) continue;
         const int e = static_cast<int>((__float_as_uint(mx) >> 23) & 0xff) - 126;
-        int xi = 0;
+        uint32_t p2 = 0, p1 = 0, p0 = 0;
         float sc = 0.0f;
         if (mx > 0.0f && e >= -104) {
             const float up = __uint_as_float(static_cast<uint32_t>(127 + 22 - e) << 23);
             sc = __uint_as_float(static_cast<uint32_t>(127 + e - 22) << 23);
-            xi = __float2int_rn(v * up);
+#pragma unroll
+            for (int k = 0; k < 4; ++k) {
+                const int xi = RoundSmall(y[k] * up);
+                const int d0 = (xi << 24) >> 24;
+                const int x1 = (xi - d0) >> 8;
+                const int d1 = (x1 << 24) >> 24;
+                const int d2 = (x1 - d1) >> 8;
+                p2 |= (static_cast<uint32_t>(d2) & 0xffu) << (8 * k);
+                p1 |= (static_cast<uint32_t>(d1) & 0xffu) << (8 * k);
+                p0 |= (static_cast<uint32_t>(d0) & 0xffu) << (8 * k);
+            }
         }
-        const int d0 = (xi << 24) >> 24;
-        const int x1 = (xi - d0) >> 8;
-        const int d1 = (x1 << 24) >> 24;
-        const int d2 = (x1 - d1) >> 8;
-        int8_t* base = dig + b * 32 + lane;
-        base[0] = static_cast<int8_t>(d2);
-        base[dstride] = static_cast<int8_t>(d1);
-        base[2 * dstride] = static_cast<int8_t>(d0);
-        base[3 * dstride] = 0;
-        if (lane == 0) sx[b] = sc;
+        uint32_t* base = reinterpret_cast<uint32_t*>(dig + 4 * i);
+        base[0] = p2;
+        base[dstride / 4] = p1;
+        base[2 * (dstride / 4)] = p0;
+        base[3 * (dstride / 4)] = 0u;
+        if ((threadIdx.x & 7) == 0) sx[i / 8] = sc;
     }
     ConsumerBar();
 }
@@ -183,7 +320,8 @@ __device__ void DigitsMk(const float* x, int nb, int8_t* dig, int dstride, float
 // ---------------------------------------------------------------- MMA pieces
 struct LaneMma {
     uint32_t lrow;  // ldmatrix row offset inside a chunk
-    float cw0, cw1; // digit weights of this lane's two columns (M = 1)
+    int m;          // integer weight of column 2t against column 2t + 1 (256 or 1)
+    float lf;       // the lane's digit factor (256 for t = 0, 1 otherwise)
     int g, t;
 };
 
@@ -196,52 +334,149 @@ __device__ __forceinline__ LaneMma MakeLane() {
     const int row = (lane & 7) + 8 * (mi & 1);
     const int half = mi >> 1;
     l.lrow = 32 * row + 16 * (half ^ ((row >> 2) & 1));
-    l.cw0 = l.t == 0 ? 65536.0f : (l.t == 1 ? 1.0f : 0.0f);
-    l.cw1 = l.t == 0 ? 256.0f : 0.0f;
+    l.m = l.t == 0 ? 256 : 1;
+    l.lf = l.t == 0 ? 256.0f : 1.0f;
     return l;
 }
 
-// One chunk (16 rows x 32 inputs) times one block of digits: adds the scaled
-// contributions of rows g and g + 8 (before the lane-pair combine).
-__device__ __forceinline__ void ChunkMma(const LaneMma& L, const uint8_t* chunk, const int8_t* dblk,
-                                         int dstride, float sxb, float& vg, float& vg8) {
-    uint32_t a0, a1, a2, a3;
-    LdMatrixX4(SmemAddr(chunk) + L.lrow, a0, a1, a2, a3);
-    uint32_t b0 = 0, b1 = 0;
-    if (L.g < 4) {
-        const int8_t* dp = dblk + L.g * dstride + 4 * L.t;
-        b0 = *reinterpret_cast<const uint32_t*>(dp);
-        b1 = *reinterpret_cast<const uint32_t*>(dp + 16);
-    }
-    int c0, c1, c2, c3;
-    MmaS8(c0, c1, c2, c3, a0, a1, a2, a3, b0, b1);
-    const float dg = HalfBits(*reinterpret_cast<const uint16_t*>(chunk + 512 + 2 * L.g));
-    const float dg8 = HalfBits(*reinterpret_cast<const uint16_t*>(chunk + 512 + 2 * (L.g + 8)));
-    const float v0 = fmaf(static_cast<float>(c1), L.cw1, static_cast<float>(c0) * L.cw0);
-    const float v1 = fmaf(static_cast<float>(c3), L.cw1, static_cast<float>(c2) * L.cw0);
-    vg = fmaf(v0, dg * sxb, vg);
-    vg8 = fmaf(v1, dg8 * sxb, vg8);
+// Up to N chunks (16 rows x 32 inputs each) times their blocks of digits:
+// chunk i at ch + i * ch_step, digits at db + i * db_step, block scale
+// sx[i * sx_step]; adds the scaled contributions of rows g and g + 8 of chunk i
+// to vg[i], vg8[i] (before the lane-pair combine).  The asm statements keep
+// program order, so the N ldmatrix loads are issued back to back, then the N
+// MMAs, then the scaling: N products in flight instead of one.
+// Products of one chunk (16 rows x 32 inputs) with the 4 digit columns of one
+// x block (D2, D1, D0, 0) land in lane (g, t) as c0 = col 2t, c1 = col 2t + 1
+// of rows g and g + 8.  Lane t = 0 holds D2 and D1, whose weights 65536 and
+// 256 are 256 * (256, 1): it forms 256 * c0 + c1 (|.| < 2^28, exact in int32)
+// and scales by 256; lane t = 1 holds D0 (weight 1) and the zero column;
+// lanes t = 2, 3 hold zero columns.  So every lane computes c0 * m + c1 in
+// integer and one conversion per row, with m and the lane factor in LaneMma.
+__device__ __forceinline__ float LaneDigits(const LaneMma& L, int c0, int c1) {
+    return __int2float_rn(c0 * L.m + c1);
 }
 
-// Row tiles of a stage (tiles_in_stage x nb chunks, row-tile major) against
-// the digits of xs; the eight warps split the work by (tile, block); results
-// (one value per row) land in s.red as [warp][tile * 16 + row].  Returns with
-// the partials written (no barrier).
-__device__ void RowTilesDot(const MkSmem& s, const LaneMma& L, const uint8_t* stage, int ntile, int nb,
-                            int dstride) {
-    const int warp = threadIdx.x >> 5;
-    const int wpt = kMkConsumerWarps / ntile;  // warps per tile (ntile in {1, 2})
-    const int tile = warp / wpt, part = warp % wpt;
-    float vg = 0.0f, vg8 = 0.0f;
-    const uint8_t* tb = stage + size_t(tile) * nb * kR16Chunk;
-    for (int b = part; b < nb; b += wpt)
-        ChunkMma(L, tb + size_t(b) * kR16Chunk, s.dig + b * 32, dstride, s.sx[b], vg, vg8);
-    vg += __shfl_xor_sync(0xffffffffu, vg, 1);
-    vg8 += __shfl_xor_sync(0xffffffffu, vg8, 1);
-    if (L.t == 0) {
-        s.red[warp * 32 + tile * 16 + L.g] = vg;
-        s.red[warp * 32 + tile * 16 + L.g + 8] = vg8;
+__device__ __forceinline__ uint32_t LdsU32(uint32_t a) {
+    uint32_t v;
+    asm volatile("ld.shared.u32 %0, [%1];" : "=r"(v) : "r"(a));
+    return v;
+}
+
+__device__ __forceinline__ float LdsF32(uint32_t a) {
+    float v;
+    asm volatile("ld.shared.f32 %0, [%1];" : "=f"(v) : "r"(a));
+    return v;
+}
+
+__device__ __forceinline__ float LdsHalf(uint32_t a) {
+    uint16_t h;
+    asm volatile("ld.shared.u16 %0, [%1];" : "=h"(h) : "r"(a));
+    return HalfBits(h);
+}
+
+// Exactly N chunks (16 rows x 32 inputs) against their digit blocks, summed:
+// chunk i at shared address ch + i * ch_step, this lane's B fragment at
+// db + i * db_step (db = digit block + g * dstride + 4 t; lanes g >= 4 hold
+// the zero columns and load nothing), block scale at sx + 4 * i * sx_step.
+// Adds rows g and g + 8 (without the lane factor L.lf, before the lane-pair
+// combine) to v, v8.  The asm statements keep program order, so the N ldmatrix
+// loads go out back to back, then the N MMAs, then the scaling.
+template <int N>
+__device__ __forceinline__ void RowChunks(const LaneMma& L, uint32_t ch, int ch_step, uint32_t db, int db_step,
+                                          uint32_t sx, int sx_step, float& v, float& v8) {
+    uint32_t a[N][4], b[N][2];
+#pragma unroll
+    for (int i = 0; i < N; ++i) LdMatrixX4(ch + i * ch_step + L.lrow, a[i][0], a[i][1], a[i][2], a[i][3]);
+#pragma unroll
+    for (int i = 0; i < N; ++i) {
+        b[i][0] = b[i][1] = 0;
+        if (L.g < 4) {
+            b[i][0] = LdsU32(db + i * db_step);
+            b[i][1] = LdsU32(db + i * db_step + 16);
+        }
     }
+    int c[N][4];
+#pragma unroll
+    for (int i = 0; i < N; ++i)
+        MmaS8(c[i][0], c[i][1], c[i][2], c[i][3], a[i][0], a[i][1], a[i][2], a[i][3], b[i][0], b[i][1]);
+#pragma unroll
+    for (int i = 0; i < N; ++i) {
+        const uint32_t sc = ch + i * ch_step + 512 + 2 * L.g;
+        const float s = LdsF32(sx + 4 * i * sx_step);
+        v = fmaf(LaneDigits(L, c[i][0], c[i][1]), LdsHalf(sc) * s, v);
+        v8 = fmaf(LaneDigits(L, c[i][2], c[i][3]), LdsHalf(sc + 16) * s, v8);
+    }
+}
+
+// Exactly N chunks (ch + i * ch_step) against one digit block (B fragment
+// b0, b1 and scale s already loaded): rows g and g + 8 of chunk i into
+// vg[i], vg8[i] (without the lane factor).
+template <int N>
+__device__ __forceinline__ void ColumnChunks(const LaneMma& L, uint32_t ch, int ch_step, uint32_t b0, uint32_t b1,
+                                             float s, float* vg, float* vg8) {
+    uint32_t a[N][4];
+#pragma unroll
+    for (int i = 0; i < N; ++i) LdMatrixX4(ch + i * ch_step + L.lrow, a[i][0], a[i][1], a[i][2], a[i][3]);
+    int c[N][4];
+#pragma unroll
+    for (int i = 0; i < N; ++i) MmaS8(c[i][0], c[i][1], c[i][2], c[i][3], a[i][0], a[i][1], a[i][2], a[i][3], b0, b1);
+#pragma unroll
+    for (int i = 0; i < N; ++i) {
+        const uint32_t sc = ch + i * ch_step + 512 + 2 * L.g;
+        vg[i] = LaneDigits(L, c[i][0], c[i][1]) * (LdsHalf(sc) * s);
+        vg8[i] = LaneDigits(L, c[i][2], c[i][3]) * (LdsHalf(sc + 16) * s);
+    }
+}
+
+// count (1..8) blocks by RowChunks with an exact compile-time count.
+__device__ __forceinline__ void RowChunksN(int count, const LaneMma& L, uint32_t ch, int ch_step, uint32_t db,
+                                           int db_step, uint32_t sx, int sx_step, float& v, float& v8) {
+    switch (count) {
+        case 8: RowChunks<8>(L, ch, ch_step, db, db_step, sx, sx_step, v, v8); break;
+        case 7: RowChunks<7>(L, ch, ch_step, db, db_step, sx, sx_step, v, v8); break;
+        case 6: RowChunks<6>(L, ch, ch_step, db, db_step, sx, sx_step, v, v8); break;
+        case 5: RowChunks<5>(L, ch, ch_step, db, db_step, sx, sx_step, v, v8); break;
+        case 4: RowChunks<4>(L, ch, ch_step, db, db_step, sx, sx_step, v, v8); break;
+        case 3: RowChunks<3>(L, ch, ch_step, db, db_step, sx, sx_step, v, v8); break;
+        case 2: RowChunks<2>(L, ch, ch_step, db, db_step, sx, sx_step, v, v8); break;
+        default: RowChunks<1>(L, ch, ch_step, db, db_step, sx, sx_step, v, v8); break;
+    }
+}
+
+constexpr int kMkMmaBatch = 8;  // chunks a warp has in flight
+
+// Row tiles of a stage (NTILE x nb chunks, row-tile major) against the digits
+// of xs; warps split the work by (tile, block); results (one value per row)
+// land in red as [warp][tile * 16 + row].  Returns with the partials written
+// (no barrier).
+template <int NTILE>
+__device__ __forceinline__ void RowTilesDotImpl(const int8_t* dig, const float* sxv, float* red, const LaneMma L,
+                                                const uint8_t* stage, int nb, int dstride) {
+    const int warp = threadIdx.x >> 5;
+    constexpr int wpt = kMkConsumerWarps / NTILE;  // warps per tile
+    const int tile = warp / wpt, part = warp % wpt;
+    const uint32_t tb = SmemAddr(stage) + tile * nb * kR16Chunk;
+    const uint32_t dl = SmemAddr(dig) + L.g * dstride + 4 * L.t;
+    const uint32_t sl = SmemAddr(sxv);
+    float v = 0.0f, v8 = 0.0f;
+    int count = part < nb ? (nb - part + wpt - 1) / wpt : 0;  // blocks part, part + wpt, ...
+    for (int b = part; count > 0; b += kMkMmaBatch * wpt, count -= kMkMmaBatch)
+        RowChunksN(min(count, kMkMmaBatch), L, tb + b * kR16Chunk, wpt * kR16Chunk, dl + b * 32, wpt * 32,
+                   sl + 4 * b, wpt, v, v8);
+    v *= L.lf;
+    v8 *= L.lf;
+    v += __shfl_xor_sync(0xffffffffu, v, 1);
+    v8 += __shfl_xor_sync(0xffffffffu, v8, 1);
+    if (L.t == 0) {
+        red[warp * 32 + tile * 16 + L.g] = v;
+        red[warp * 32 + tile * 16 + L.g + 8] = v8;
+    }
+}
+
+__device__ __forceinline__ void RowTilesDot(const MkSmem& s, const LaneMma& L, const uint8_t* stage, int ntile,
+                                            int nb, int dstride) {
+    if (ntile == 2) RowTilesDotImpl<2>(s.dig, s.sx, s.red, L, stage, nb, dstride);
+    else RowTilesDotImpl<1>(s.dig, s.sx, s.red, L, stage, nb, dstride);
 }
 
 // Sum of the partials of row r of tile `tile` (after a barrier).
@@ -253,31 +488,102 @@ __device__ __forceinline__ float RowTotal(const MkSmem& s, int ntile, int tile, 
 }
 
 // A block column (ntiles chunks of 16 rows x 32 inputs) times one block of
-// digits: out[row] += value (+ addend[row]) by red.add; a warp per row tile.
-__device__ void ColumnDotAdd(const LaneMma& L, const uint8_t* column, int ntiles, int nrows,
-                             const int8_t* dblk, int dstride, float sxb, float* out,
-                             const float* addend) {
+// digits (scale *sxb), added into acc[row] in shared memory (each row has one
+// owner lane, so no atomics); warp w takes row tiles w, w + 8, ...
+__device__ __forceinline__ void ColumnDotSmem(const LaneMma L, const uint8_t* column, int ntiles, int nrows,
+                                              const int8_t* dblk, int dstride, const float* sxb, float* acc) {
     const int warp = threadIdx.x >> 5;
-    for (int t = warp; t < ntiles; t += kMkConsumerWarps) {
-        float vg = 0.0f, vg8 = 0.0f;
-        ChunkMma(L, column + size_t(t) * kR16Chunk, dblk, dstride, sxb, vg, vg8);
-        vg += __shfl_xor_sync(0xffffffffu, vg, 1);
-        vg8 += __shfl_xor_sync(0xffffffffu, vg8, 1);
-        if (L.t == 0) {
-            const int r0 = t * 16 + L.g, r1 = r0 + 8;
-            if (r0 < nrows) RedAdd(out + r0, vg + (addend ? __ldcg(addend + r0) : 0.0f));
-            if (r1 < nrows) RedAdd(out + r1, vg8 + (addend ? __ldcg(addend + r1) : 0.0f));
+    uint32_t b0 = 0, b1 = 0;
+    if (L.g < 4) {
+        const uint32_t db = SmemAddr(dblk) + L.g * dstride + 4 * L.t;
+        b0 = LdsU32(db);
+        b1 = LdsU32(db + 16);
+    }
+    const float s = *sxb;
+    const uint32_t col = SmemAddr(column);
+    for (int t0 = warp; t0 < ntiles; t0 += kMkMmaBatch * kMkConsumerWarps) {
+        const int count = min(kMkMmaBatch, (ntiles - t0 + kMkConsumerWarps - 1) / kMkConsumerWarps);
+        float vg[kMkMmaBatch], vg8[kMkMmaBatch];
+        const uint32_t ch = col + t0 * kR16Chunk;
+        constexpr int st = kMkConsumerWarps * kR16Chunk;
+        switch (count) {
+            case 8: ColumnChunks<8>(L, ch, st, b0, b1, s, vg, vg8); break;
+            case 7: ColumnChunks<7>(L, ch, st, b0, b1, s, vg, vg8); break;
+            case 6: ColumnChunks<6>(L, ch, st, b0, b1, s, vg, vg8); break;
+            case 5: ColumnChunks<5>(L, ch, st, b0, b1, s, vg, vg8); break;
+            case 4: ColumnChunks<4>(L, ch, st, b0, b1, s, vg, vg8); break;
+            case 3: ColumnChunks<3>(L, ch, st, b0, b1, s, vg, vg8); break;
+            case 2: ColumnChunks<2>(L, ch, st, b0, b1, s, vg, vg8); break;
+            default: ColumnChunks<1>(L, ch, st, b0, b1, s, vg, vg8); break;
+        }
+#pragma unroll
+        for (int i = 0; i < kMkMmaBatch; ++i) {
+            if (i >= count) break;
+            float a = vg[i] * L.lf, a8 = vg8[i] * L.lf;
+            a += __shfl_xor_sync(0xffffffffu, a, 1);
+            a8 += __shfl_xor_sync(0xffffffffu, a8, 1);
+            const int r0 = (t0 + i * kMkConsumerWarps) * 16 + L.g, r1 = r0 + 8;
+            if (L.t == 0 && r0 < nrows) acc[r0] += a;
+            if (L.t == 0 && r1 < nrows) acc[r1] += a8;
         }
     }
 }
 
+// After a barrier: out[i] += acc[i] (+ addend[i]) for i < n by red.add, one
+// coalesced pass, and acc back to zero.
+__device__ __forceinline__ void FlushRed(float* acc, float* out, int n, const float* addend) {
+    for (int i = threadIdx.x; i < n; i += 256) {
+        RedAdd(out + i, acc[i] + (addend ? __ldcg(addend + i) : 0.0f));
+        acc[i] = 0.0f;
+    }
+}
+
+// Digit planes of one 32-block held by a warp (lane = element): block scale
+// into *sxp.  Same digits as RmsNormDigits / DigitsMk.
+__device__ __forceinline__ void DigitsWarp(float v, int8_t* dblk, int dstride, float* sxp) {
+    const int lane = threadIdx.x & 31;
+    const float mx = WarpMax(fabsf(v));
+    const int e = static_cast<int>((__float_as_uint(mx) >> 23) & 0xff) - 126;
+    int xi = 0;
+    float sc = 0.0f;
+    if (mx > 0.0f && e >= -104) {
+        const float up = __uint_as_float(static_cast<uint32_t>(127 + 22 - e) << 23);
+        sc = __uint_as_float(static_cast<uint32_t>(127 + e - 22) << 23);
+        xi = RoundSmall(v * up);
+    }
+    const int d0 = (xi << 24) >> 24;
+    const int x1 = (xi - d0) >> 8;
+    const int d1 = (x1 << 24) >> 24;
+    const int d2 = (x1 - d1) >> 8;
+    dblk[lane] = static_cast<int8_t>(d2);
+    dblk[dstride + lane] = static_cast<int8_t>(d1);
+    dblk[2 * dstride + lane] = static_cast<int8_t>(d0);
+    dblk[3 * dstride + lane] = 0;
+    if (lane == 0) *sxp = sc;
+}
+
 // ---------------------------------------------------------------- schedule
-// The chunk sequence of one CTA for one step; the producer issues it, the
-// consumers consume it, in the same order.
-struct Chunk {
-    const uint8_t* src;
-    uint32_t bytes;
-};
+// The chunk sequence of one CTA for one step (weights only, so every step
+// repeats it); thread 0 issues it into the ring, the consumers consume it, in
+// the same order.
+
+// FFN-B share of CTA c: the row-major chunk indices [q0, q1) of the R16 down
+// weight (ceil(dim/16) row tiles x hidden/32 blocks), equal to within one
+// chunk for every CTA, visited as pieces (row tile t, blocks b .. b+len-1)
+// of at most one row tile and one ring stage each.
+template <typename F>
+__device__ __forceinline__ void ForEachDownPiece(const MegaParams& p, int c, int G, F&& f) {
+    const int nj = p.hidden / 32;
+    const long long Q = static_cast<long long>((p.dim + 15) / 16) * nj;
+    const int q0 = static_cast<int>(Q * c / G), q1 = static_cast<int>(Q * (c + 1) / G);
+    const int smax = p.stage_bytes / kR16Chunk;
+    for (int q = q0; q < q1;) {
+        const int t = q / nj, b = q - t * nj;
+        const int len = min(min(q1 - q, nj - b), smax);
+        f(t, b, len);
+        q += len;
+    }
+}
 
 template <typename F>
 __device__ void ForEachChunk(const MegaParams& p, int c, int G, F&& f) {
@@ -288,6 +594,7 @@ __device__ void ForEachChunk(const MegaParams& p, int c, int G, F&& f) {
     const int ntiles_dim = (p.dim + 15) / 16;
     const uint32_t col_b = static_cast<uint32_t>(ntiles_dim) * kR16Chunk;
     const int nj = p.hidden / 32;
+    const int t_h = p.hidden / 16;
     const int t_lm = (p.vocab + 15) / 16;
     const int bph = p.hd / 32;  // wo block columns per head
     for (int l = 0; l < p.n_layers; ++l) {
@@ -295,52 +602,27 @@ __device__ void ForEachChunk(const MegaParams& p, int c, int G, F&& f) {
         for (int t = c; t < t_qkv; t += G) {
             const int seg = t < tq ? 0 : (t < tq + tk ? 1 : 2);
             const int ti = seg == 0 ? t : (seg == 1 ? t - tq : t - tq - tk);
-            f(Chunk{L.wqkv[seg] + size_t(ti) * tile_b, tile_b});
+            f(Chunk{L.wqkv[seg] + size_t(ti) * tile_b, nullptr, tile_b, 0});
         }
         for (int h = G - 1 - c; h < p.n_heads; h += G)
             for (int j = 0; j < bph; ++j)
-                f(Chunk{L.wo + size_t(h * bph + j) * col_b, col_b});
-        for (int j = c; j < nj; j += G) {
-            f(Chunk{L.gate + size_t(2 * j) * tile_b, 2 * tile_b});
-            f(Chunk{L.up + size_t(2 * j) * tile_b, 2 * tile_b});
-            f(Chunk{L.down + size_t(j) * col_b, col_b});
-        }
+                f(Chunk{L.wo + size_t(h * bph + j) * col_b, nullptr, col_b, 0});
+        // FFN-A: gate row tile t and up row tile t in one stage
+        for (int t = c; t < t_h; t += G)
+            f(Chunk{L.gate + size_t(t) * tile_b, L.up + size_t(t) * tile_b, tile_b, tile_b});
+        // FFN-B: this CTA's share of the down rows, in pieces of one row tile
+        ForEachDownPiece(p, c, G, [&](int t, int b, int len) {
+            f(Chunk{L.down + (size_t(t) * nj + b) * kR16Chunk, nullptr, static_cast<uint32_t>(len) * kR16Chunk, 0});
+        });
     }
     // lm_head: two row tiles per stage
     for (int t2 = c; 2 * t2 < t_lm; t2 += G)
-        f(Chunk{p.lm_head + size_t(2 * t2) * tile_b, (2 * t2 + 1 < t_lm ? 2u : 1u) * tile_b});
-}
-
-__device__ void Producer(const MegaParams& p, const MkSmem& s) {
-    if ((threadIdx.x & 31) != 0) return;
-    const int G = gridDim.x, c = blockIdx.x;
-    unsigned n = 0;
-    bool abort = false;
-    for (int step = 0; step < p.n_steps && !abort; ++step) {
-        ForEachChunk(p, c, G, [&](const Chunk& ch) {
-            if (abort) return;
-            const int slot = n % kMkStages;
-            if (n >= static_cast<unsigned>(kMkStages)) {
-                if (!MbarWaitFor(&s.empty[slot], ((n / kMkStages) - 1) & 1, kMkWaitNs, s.flags)) {
-                    abort = true;
-                    atomicCAS(p.status, 0, MLB_ERR_DEVICE_TIMEOUT);
-                    return;
-                }
-            }
-            MbarExpectTx(&s.full[slot], ch.bytes);
-            BulkLoad(s.ring + size_t(slot) * p.stage_bytes, ch.src, ch.bytes, &s.full[slot]);
-            ++n;
-        });
-    }
-    // Drain: wait (bounded) until every stage issued has landed, so no copy
-    // into this CTA's shared memory is in flight when it exits.
-    const unsigned first = n > static_cast<unsigned>(kMkStages) ? n - kMkStages : 0;
-    for (unsigned k = first; k < n; ++k)
-        MbarWaitFor(&s.full[k % kMkStages], (k / kMkStages) & 1, kMkWaitNs, nullptr);
+        f(Chunk{p.lm_head + size_t(2 * t2) * tile_b, nullptr, (2 * t2 + 1 < t_lm ? 2u : 1u) * tile_b, 0});
 }
 
 // ---------------------------------------------------------------- consumers
-__device__ void Consumers(const MegaParams& p, const MkSmem& s) {
+// Returns how many chunks it consumed (all of them unless it aborted).
+__device__ unsigned Consumers(const MegaParams& p, const MkSmem& s) {
     const int G = gridDim.x, c = blockIdx.x;
     const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
     const LaneMma L = MakeLane();
@@ -351,14 +633,26 @@ __device__ void Consumers(const MegaParams& p, const MkSmem& s) {
     const int t_qkv = tq + 2 * tk;
     const int ntiles_dim = (p.dim + 15) / 16;
     const int nj = p.hidden / 32;
+    const int t_h = p.hidden / 16;
     const int t_lm = (p.vocab + 15) / 16;
     const int bph = p.hd / 32;
     // signals per step: one per QKV worker CTA, one per head, one per FFN
     // worker CTA; every CTA takes one LM ticket
-    const unsigned w_qkv = WorkerCount(G, t_qkv), w_att = p.n_heads, w_ffn = WorkerCount(G, nj),
-                   w_lm = G;
-    const int ctr_lm_ticket = 3 * p.n_layers, ctr_token = 3 * p.n_layers + 1;
-    unsigned n = 0;  // chunk counter (same sequence as the producer)
+    // FFN-B shares: the CTAs with a non-empty range of the down chunks
+    const long long dQ = static_cast<long long>(ntiles_dim) * nj;
+    const int dq0 = static_cast<int>(dQ * c / G), dq1 = static_cast<int>(dQ * (c + 1) / G);
+    const bool has_down = dq1 > dq0;
+    const int nneed = min(dq1 - dq0, nj);
+    const int fdstride = DigitStride(nj);
+    const unsigned w_qkv = WorkerCount(G, t_qkv), w_att = p.n_heads, w_ffa = WorkerCount(G, t_h),
+                   w_ffb = static_cast<unsigned>(min(static_cast<long long>(G), dQ)), w_lm = G;
+    const int ctr_lm_ticket = kMkPhases * p.n_layers, ctr_token = kMkPhases * p.n_layers + 1;
+    Ring rg;  // the chunk sequence thread 0 issued in the prologue, continued here
+    rg.n = 0;
+    rg.len = static_cast<unsigned>(s.flags[2]);
+    rg.total = rg.len * static_cast<unsigned>(p.n_steps);
+    rg.li = rg.len ? kMkStages % rg.len : 0;
+    rg.pol = L2EvictFirstPolicy();
 
     for (int step = 0; step < p.n_steps; ++step) {
         const int pos = p.start_pos + step;
@@ -378,9 +672,9 @@ __device__ void Consumers(const MegaParams& p, const MkSmem& s) {
                     if (Lw.bias[seg] && tid < 4) CpAsync16(s.vec + 16 * i + 4 * tid, Lw.bias[seg] + ti * 16 + 4 * tid);
                 }
                 if (l == 0) {
-                    if (step > 0 && !WaitCounter(p, s, ctr_token, k1 - 1)) return;
-                } else if (!WaitCounter(p, s, 3 * (l - 1) + 2, k1 * w_ffn)) {
-                    return;
+                    if (step > 0 && !WaitCounter(p, s, ctr_token, k1 - 1)) return rg.n;
+                } else if (!WaitCounter(p, s, kMkPhases * (l - 1) + 3, k1 * w_ffb)) {
+                    return rg.n;
                 }
                 Trace(p, step, l, 0);
                 if (l == 0) {
@@ -403,18 +697,16 @@ __device__ void Consumers(const MegaParams& p, const MkSmem& s) {
                         xout[i] = 0.0f;
                     }
                 }
-                RmsNormSmem(s.xs, s.nw, p.dim, p.eps, s.scratch);
-                DigitsMk(s.xs, nb_dim, s.dig, dstride, s.sx);
+                RmsNormDigits(s.xs, s.nw, p.dim, p.eps, s.dig, dstride, s.sx, s.scratch);
                 Trace(p, step, l, 11);
                 for (int t = c, i = 0; t < t_qkv; t += G, ++i) {
                     const int seg = t < tq ? 0 : (t < tq + tk ? 1 : 2);
                     const int ti = seg == 0 ? t : (seg == 1 ? t - tq : t - tq - tk);
                     const int rows = seg == 0 ? p.qd : p.kd;
                     const int off = seg == 0 ? 0 : (seg == 1 ? p.qd : p.qd + p.kd);
-                    if (!WaitChunk(p, s, n)) return;
-                    RowTilesDot(s, L, s.ring + size_t(n % kMkStages) * p.stage_bytes, 1, nb_dim, dstride);
-                    ReleaseChunk(s, n);
-                    ++n;
+                    WaitChunk(p, s, rg);
+                    RowTilesDot(s, L, StagePtr(p, s, rg), 1, nb_dim, dstride);
+                    ReleaseChunk(p, s, rg);
                     if (tid < 16) {
                         const int r = ti * 16 + tid;
                         if (r < rows) {
@@ -426,7 +718,7 @@ __device__ void Consumers(const MegaParams& p, const MkSmem& s) {
                     ConsumerBar();
                 }
                 Trace(p, step, l, 10);
-                Signal(p, 3 * l + 0);
+                Signal(p, kMkPhases * l + 0);
                 Trace(p, step, l, 1);
             }
             // ---------------- attention + O projection, one query head
@@ -434,17 +726,28 @@ __device__ void Consumers(const MegaParams& p, const MkSmem& s) {
                 const int hd = p.hd, half = hd / 2, kvh = h / p.group;
                 const size_t pstride = size_t(p.n_kv) * hd;
                 const size_t lbase = size_t(l) * p.max_seq * pstride + size_t(kvh) * hd;
-                // pull this head's cached K and V rows into L2 while QKV runs
-                for (int pp = tid; pp < 2 * pos; pp += 256) {
-                    const float* row = (pp < pos ? p.kc : p.vc) + lbase + size_t(pp < pos ? pp : pp - pos) * pstride;
-                    BulkPrefetchL2(row, static_cast<uint32_t>(hd) * 4);
+                const int lpr = hd / 4, rpi = 32 / lpr;  // float4 lanes per K/V row, rows per warp pass
+                // While QKV runs: the K row of cached position tid (first chunk)
+                // into registers (its first 64 floats), and every V row plus
+                // the K rows of later chunks into L2.  None depend on this step.
+                float4 kpre[16];
+                {
+                    const bool kp = tid < pos;
+                    const float4* kr = reinterpret_cast<const float4*>(p.kc + lbase + size_t(kp ? tid : 0) * pstride);
+#pragma unroll
+                    for (int i = 0; i < 16; ++i)
+                        kpre[i] = kp && i < lpr ? __ldcg(kr + i) : make_float4(0.f, 0.f, 0.f, 0.f);
                 }
+                for (int pp = tid; pp < pos; pp += 256)
+                    BulkPrefetchL2(p.vc + lbase + size_t(pp) * pstride, static_cast<uint32_t>(hd) * 4);
+                for (int pp = kMkAttnChunk + tid; pp < pos; pp += 256)
+                    BulkPrefetchL2(p.kc + lbase + size_t(pp) * pstride, static_cast<uint32_t>(hd) * 4);
                 // RoPE rows of this position (s.att is free until the values pass)
                 float* ct = s.att;
                 float* st = s.att + half;
                 LoadVecCg(ct, p.rope_cos + size_t(pos) * half, half);
                 LoadVecCg(st, p.rope_sin + size_t(pos) * half, half);
-                if (!WaitCounter(p, s, 3 * l + 0, k1 * w_qkv)) return;
+                if (!WaitCounter(p, s, kMkPhases * l + 0, k1 * w_qkv)) return rg.n;
                 Trace(p, step, l, 2);
                 float* q = s.vec;
                 float* kn = s.vec + 128;
@@ -478,7 +781,6 @@ __device__ void Consumers(const MegaParams& p, const MkSmem& s) {
                 // Scores: a thread per position (its K row as float4 loads, all
                 // in flight together).  Values: a warp per 32 positions, lanes
                 // over (row, float4 column), every row load in flight together.
-                const int lpr = hd / 4, rpi = 32 / lpr;  // lanes per row, rows per pass
                 const int rsub = lane / lpr, col = lane % lpr;
                 float m_run = -INFINITY, l_run = 0.0f;
                 for (int base = 0; base <= pos; base += kMkAttnChunk) {
@@ -498,7 +800,20 @@ __device__ void Consumers(const MegaParams& p, const MkSmem& s) {
                                 dot = fmaf(qv.w, kv.w, dot);
                             }
                         } else {
-                            for (int i0 = 0; i0 < lpr; i0 += 8) {  // 8 loads in flight
+                            int i0 = 0;
+                            if (base == 0) {  // the prefetched part of the row
+#pragma unroll
+                                for (int i = 0; i < 16; ++i)
+                                    if (i < lpr) {
+                                        const float4 qv = q4[i];
+                                        dot = fmaf(qv.x, kpre[i].x, dot);
+                                        dot = fmaf(qv.y, kpre[i].y, dot);
+                                        dot = fmaf(qv.z, kpre[i].z, dot);
+                                        dot = fmaf(qv.w, kpre[i].w, dot);
+                                    }
+                                i0 = 16;
+                            }
+                            for (; i0 < lpr; i0 += 8) {  // 8 loads in flight
                                 float4 kv[8];
 #pragma unroll
                                 for (int i = 0; i < 8; ++i)
@@ -589,81 +904,107 @@ __device__ void Consumers(const MegaParams& p, const MkSmem& s) {
                     }
                     ConsumerBar();
                 }
-                for (int d = tid; d < hd; d += 256) o[d] = o[d] / l_run;
-                Trace(p, step, l, 8);
+                // the normalised output's digit planes, straight from the
+                // warps that hold it (warp w: block w; hd is a multiple of 32)
+                for (int d = tid; d < hd; d += 256)
+                    DigitsWarp(o[d] / l_run, s.vdig + (d >> 5) * 32, vstride, s.vsx + (d >> 5));
                 ConsumerBar();
-                DigitsMk(o, bph, s.vdig, vstride, s.vsx);
+                Trace(p, step, l, 8);
+                // wo block columns of the head into acc, then one red.add pass
                 for (int j = 0; j < bph; ++j) {
-                    if (!WaitChunk(p, s, n)) return;
-                    ColumnDotAdd(L, s.ring + size_t(n % kMkStages) * p.stage_bytes, ntiles_dim, p.dim,
-                                 s.vdig + j * 32, vstride, s.vsx[j], p.xmid, nullptr);
-                    ReleaseChunk(s, n);
-                    ++n;
+                    WaitChunk(p, s, rg);
+                    ColumnDotSmem(L, StagePtr(p, s, rg), ntiles_dim, p.dim,
+                                  s.vdig + j * 32, vstride, s.vsx + j, s.acc);
+                    ReleaseChunk(p, s, rg);
                 }
+                FlushRed(s.acc, p.xmid, p.dim, nullptr);
                 Trace(p, step, l, 9);
-                Signal(p, 3 * l + 1);
+                Signal(p, kMkPhases * l + 1);
                 Trace(p, step, l, 3);
             }
-            // ---------------- FFN: gate/up rows of a hidden block, SwiGLU, w_down column
-            if (c < nj) {
+            // ---------------- FFN-A: gate and up row tiles, SwiGLU -> ff
+            if (c < t_h) {
                 LoadVecCg(s.nw, Lw.ffn_norm, p.dim);  // independent of the wait
-                if (!WaitCounter(p, s, 3 * l + 1, k1 * w_att)) return;
+                if (!WaitCounter(p, s, kMkPhases * l + 1, k1 * w_att)) return rg.n;
                 Trace(p, step, l, 4);
                 LoadVecCg(s.xs, p.xmid, p.dim);
                 CpAsyncWaitAll();
                 ConsumerBar();
-                RmsNormSmem(s.xs, s.nw, p.dim, p.eps, s.scratch);
-                DigitsMk(s.xs, nb_dim, s.dig, dstride, s.sx);
+                RmsNormDigits(s.xs, s.nw, p.dim, p.eps, s.dig, dstride, s.sx, s.scratch);
                 Trace(p, step, l, 7);
-                float* gv = s.vec;
-                float* uv = s.vec + 32;
-                float* ff = s.vec + 64;
-                for (int j = c; j < nj; j += G) {
-                    for (int part = 0; part < 2; ++part) {
-                        if (!WaitChunk(p, s, n)) return;
-                        RowTilesDot(s, L, s.ring + size_t(n % kMkStages) * p.stage_bytes, 2, nb_dim, dstride);
-                        ReleaseChunk(s, n);
-                        ++n;
-                        if (tid < 32) (part == 0 ? gv : uv)[tid] = RowTotal(s, 2, tid >> 4, tid & 15);
-                        ConsumerBar();
-                    }
-                    if (tid < 32) {
-                        const float v = gv[tid];
-                        const float sig = 1.0f / (1.0f + expf(-v));
-                        ff[tid] = v * sig * uv[tid];
+                for (int t = c; t < t_h; t += G) {
+                    WaitChunk(p, s, rg);
+                    RowTilesDot(s, L, StagePtr(p, s, rg), 2, nb_dim, dstride);
+                    ReleaseChunk(p, s, rg);  // its barrier publishes s.red
+                    if (tid < 16) {
+                        const float g = RowTotal(s, 2, 0, tid), u = RowTotal(s, 2, 1, tid);
+                        const float sig = 1.0f / (1.0f + expf(-g));
+                        p.ff[t * 16 + tid] = g * sig * u;
                     }
                     ConsumerBar();
-                    DigitsMk(ff, 1, s.vdig, vstride, s.vsx);
-                    if (!WaitChunk(p, s, n)) return;
-                    ColumnDotAdd(L, s.ring + size_t(n % kMkStages) * p.stage_bytes, ntiles_dim, p.dim,
-                                 s.vdig, vstride, s.vsx[0], xout, j == 0 ? p.xmid : nullptr);
-                    ReleaseChunk(s, n);
-                    ++n;
                 }
-                Trace(p, step, l, 6);
-                Signal(p, 3 * l + 2);
+                Signal(p, kMkPhases * l + 2);
                 Trace(p, step, l, 5);
+            }
+            // ---------------- FFN-B: this CTA's share of the down rows, + residual
+            if (has_down) {
+                if (!WaitCounter(p, s, kMkPhases * l + 2, k1 * w_ffa)) return rg.n;
+                Trace(p, step, l, 12);
+                // the ff blocks the share touches: (q0 + i) mod nj, i < nneed
+                for (int k = tid; k < nneed * 8; k += 256) {
+                    const int b = (dq0 + k / 8) % nj, e = 4 * (k % 8);
+                    CpAsync16(s.fx + b * 32 + e, p.ff + b * 32 + e);
+                }
+                CpAsyncWaitAll();
+                ConsumerBar();
+                DigitsBlocks(s.fx, dq0 % nj, nneed, nj, s.fdig, fdstride, s.fsx);
+                int t_first = -1, t_last = -1;
+                bool res_first = false;
+                ForEachDownPiece(p, c, G, [&](int t, int b, int len) {
+                    WaitChunk(p, s, rg);
+                    RowTilesDotImpl<1>(s.fdig + b * 32, s.fsx + b, s.red, L,
+                                       StagePtr(p, s, rg), len, fdstride);
+                    ReleaseChunk(p, s, rg);  // its barrier publishes s.red
+                    if (t_first < 0) {
+                        t_first = t;
+                        res_first = b == 0;
+                    }
+                    t_last = t;
+                    if (tid < 16) s.acc[t * 16 + tid] += RowTotal(s, 1, 0, tid);
+                    ConsumerBar();
+                });
+                Trace(p, step, l, 6);
+                // the CTA whose share starts a row tile at block 0 adds x_mid
+                for (int t = t_first; t <= t_last; ++t)
+                    if (tid < 16) {
+                        const int r = t * 16 + tid;
+                        if (r < p.dim) {
+                            const bool res = t > t_first || res_first;
+                            RedAdd(xout + r, s.acc[r] + (res ? __ldcg(p.xmid + r) : 0.0f));
+                        }
+                        s.acc[r] = 0.0f;
+                    }
+                Signal(p, kMkPhases * l + 3);
+                Trace(p, step, l, 13);
             }
         }
         // ---------------- lm_head + arg-max
         LoadVecCg(s.nw, p.final_norm, p.dim);  // independent of the wait
-        if (!WaitCounter(p, s, 3 * (p.n_layers - 1) + 2, k1 * w_ffn)) return;
+        if (!WaitCounter(p, s, kMkPhases * (p.n_layers - 1) + 3, k1 * w_ffb)) return rg.n;
         Trace(p, step, p.n_layers, 0);
         float* xfin = p.xbuf[p.n_layers & 1];
         LoadVecCg(s.xs, xfin, p.dim);
         CpAsyncWaitAll();
         ConsumerBar();
-        RmsNormSmem(s.xs, s.nw, p.dim, p.eps, s.scratch);
-        DigitsMk(s.xs, nb_dim, s.dig, dstride, s.sx);
+        RmsNormDigits(s.xs, s.nw, p.dim, p.eps, s.dig, dstride, s.sx, s.scratch);
         float best = -INFINITY;
         int besti = 0x7fffffff;
         for (int t2 = c; 2 * t2 < t_lm; t2 += G) {
             // a lone last tile leaves stale bytes in the stage's second half;
             // its rows are past the vocabulary and skipped
-            if (!WaitChunk(p, s, n)) return;
-            RowTilesDot(s, L, s.ring + size_t(n % kMkStages) * p.stage_bytes, 2, nb_dim, dstride);
-            ReleaseChunk(s, n);
-            ++n;
+            WaitChunk(p, s, rg);
+            RowTilesDot(s, L, StagePtr(p, s, rg), 2, nb_dim, dstride);
+            ReleaseChunk(p, s, rg);
             if (tid < 32) {
                 const int r = (2 * t2 + (tid >> 4)) * 16 + (tid & 15);
                 if (r < p.vocab) {
@@ -730,60 +1071,98 @@ __device__ void Consumers(const MegaParams& p, const MkSmem& s) {
         }
         ConsumerBar();
     }
+    return rg.n;
 }
 
-// 9 warps: one SM sub-partition holds 3 of them, so 168 registers a thread
-// at most (16384 / 96, in steps of 8)
 __global__ void __launch_bounds__(kMkThreads, 1) MegaDecodeKernel(const MegaParams p) {
     extern __shared__ __align__(128) uint8_t smem[];
     const int nb_dim = p.dim / 32;
+    // fixed-size buffers first, at compile-time offsets (their addresses
+    // need no registers), then the dim-sized ones and the ring
     MkSmem s;
-    size_t off = 0;
-    auto take = [&](size_t bytes) {
-        uint8_t* ptr = smem + off;
-        off += (bytes + 127) & ~size_t(127);
-        return ptr;
-    };
-    s.ring = take(size_t(kMkStages) * p.stage_bytes);
-    s.full = reinterpret_cast<uint64_t*>(take(8 * kMkStages));
-    s.empty = reinterpret_cast<uint64_t*>(take(8 * kMkStages));
-    s.xs = reinterpret_cast<float*>(take(4 * size_t(p.dim)));
-    s.nw = reinterpret_cast<float*>(take(4 * size_t(p.dim)));
-    s.dig = reinterpret_cast<int8_t*>(take(4 * size_t(DigitStride(nb_dim))));
-    s.sx = reinterpret_cast<float*>(take(4 * size_t(nb_dim)));
-    s.vdig = reinterpret_cast<int8_t*>(take(4 * size_t(DigitStride(4))));
-    s.vsx = reinterpret_cast<float*>(take(16));
-    s.red = reinterpret_cast<float*>(take(4 * 8 * 32));
-    s.vec = reinterpret_cast<float*>(take(4 * 512));
-    s.att = reinterpret_cast<float*>(take(4 * 8 * 128));
-    s.sc = reinterpret_cast<float*>(take(4 * kMkAttnChunk));
-    s.scratch = reinterpret_cast<float*>(take(4 * 32));
-    s.flags = reinterpret_cast<int*>(take(16));
+    s.full = reinterpret_cast<uint64_t*>(smem + kOffFull);
+    s.flags = reinterpret_cast<int*>(smem + kOffFlags);
+    s.scratch = reinterpret_cast<float*>(smem + kOffScratch);
+    s.vsx = reinterpret_cast<float*>(smem + kOffVsx);
+    s.vdig = reinterpret_cast<int8_t*>(smem + kOffVdig);
+    s.red = reinterpret_cast<float*>(smem + kOffRed);
+    s.vec = reinterpret_cast<float*>(smem + kOffVec);
+    s.att = reinterpret_cast<float*>(smem + kOffAtt);
+    s.sc = reinterpret_cast<float*>(smem + kOffSc);
+    const size_t vbytes = Round128(4 * size_t(p.dim));
+    s.xs = reinterpret_cast<float*>(smem + kOffFixedEnd);
+    s.nw = reinterpret_cast<float*>(smem + kOffFixedEnd + vbytes);
+    s.dig = reinterpret_cast<int8_t*>(smem + kOffFixedEnd + 2 * vbytes);
+    s.sx = reinterpret_cast<float*>(smem + kOffFixedEnd + 2 * vbytes + Round128(4 * size_t(DigitStride(nb_dim))));
+    s.acc = reinterpret_cast<float*>(smem + kOffFixedEnd + 2 * vbytes + Round128(4 * size_t(DigitStride(nb_dim))) +
+                                     Round128(4 * size_t(nb_dim)));
+    const int nj_all = p.hidden / 32;
+    size_t off2 = kOffFixedEnd + 3 * vbytes + Round128(4 * size_t(DigitStride(nb_dim))) + Round128(4 * size_t(nb_dim));
+    s.fx = reinterpret_cast<float*>(smem + off2);
+    off2 += Round128(4 * size_t(p.hidden));
+    s.fdig = reinterpret_cast<int8_t*>(smem + off2);
+    off2 += Round128(4 * size_t(DigitStride(nj_all)));
+    s.fsx = reinterpret_cast<float*>(smem + off2);
+    off2 += Round128(4 * size_t(nj_all));
+    const size_t list_off = off2;
+    for (int i = threadIdx.x; i < p.dim; i += kMkThreads) s.acc[i] = 0.0f;
+    s.list = reinterpret_cast<Chunk*>(smem + list_off);
+    s.ring = smem + list_off + Round128(sizeof(Chunk) * size_t(p.list_cap));
     if (threadIdx.x == 0) {
-        for (int i = 0; i < kMkStages; ++i) {
-            MbarInit(&s.full[i], 1);
-            MbarInit(&s.empty[i], 1);
-        }
+        for (int i = 0; i < kMkStages; ++i) MbarInit(&s.full[i], 1);
         FenceMbarInit();
-        s.flags[0] = 0;
-        s.flags[1] = 0;
+        for (int i = 0; i < 8; ++i) s.flags[i] = 0;
+        int len = 0;
+        ForEachChunk(p, blockIdx.x, gridDim.x, [&](const Chunk& ch) {
+            if (len < p.list_cap) s.list[len] = ch;
+            ++len;
+        });
+        s.flags[2] = len;
+        if (len > p.list_cap) {  // sized on the host (MegaListCap); an empty list is fine
+            atomicCAS(p.status, 0, MLB_ERR_UNSUPPORTED);
+            s.flags[0] = 1;
+        } else {
+            const unsigned total = static_cast<unsigned>(len) * p.n_steps;
+            const uint64_t pol = L2EvictFirstPolicy();
+            for (unsigned k = 0; k < kMkStages && k < total; ++k) IssueChunk(p, s, k, k % len, pol);
+        }
     }
     __syncthreads();
-    if (threadIdx.x >= kMkConsumerWarps * 32) {
-        Producer(p, s);  // stops early when the consumers set flags[0]
-    } else {
-        Consumers(p, s);
+    if (s.flags[0]) return;
+    Consumers(p, s);
+    // Wait (bounded) for any copy still in flight into this CTA's shared
+    // memory.  A slot never holds two copies at once (nothing is issued once
+    // the CTA aborts), so the last kMkStages issued chunks cover them all; the
+    // ones already consumed return at once.
+    ConsumerBar();
+    if (threadIdx.x == 0) {
+        const unsigned issued = static_cast<unsigned>(s.flags[5]);
+        for (unsigned k = issued > kMkStages ? issued - kMkStages : 0; k < issued; ++k)
+            MbarWaitFor(&s.full[k % kMkStages], (k / kMkStages) & 1, kMkWaitNs, nullptr);
     }
 }
 
 }  // namespace
 
+int MegaListCap(const MegaParams& p, int G) {
+    auto per = [G](int items) { return (items + G - 1) / G; };  // items of one CTA at most
+    const int t_qkv = (p.qd + 15) / 16 + 2 * ((p.kd + 15) / 16);
+    const int t_lm = (p.vocab + 15) / 16;
+    const long long dQ = static_cast<long long>((p.dim + 15) / 16) * (p.hidden / 32);
+    const int share = static_cast<int>((dQ + G - 1) / G);  // down chunks of one CTA at most
+    const int smax = p.stage_bytes / kR16Chunk;
+    const int pieces = share / min(smax, p.hidden / 32) + 2;  // + the splits at row-tile ends
+    return p.n_layers * (per(t_qkv) + per(p.n_heads) * (p.hd / 32) + per(p.hidden / 16) + pieces) +
+           per((t_lm + 1) / 2);
+}
+
 size_t MegaSmemBytes(const MegaParams& p) {
-    auto r = [](size_t b) { return (b + 127) & ~size_t(127); };
     const int nb_dim = p.dim / 32;
-    return r(size_t(kMkStages) * p.stage_bytes) + r(8 * kMkStages) * 2 + r(4 * size_t(p.dim)) * 2 +
-           r(4 * size_t(DigitStride(nb_dim))) + r(4 * size_t(nb_dim)) + r(4 * size_t(DigitStride(4))) +
-           r(16) + r(4 * 8 * 32) + r(4 * 512) + r(4 * 8 * 128) + r(4 * kMkAttnChunk) + r(4 * 32) + r(16) + 128;
+    const int nj = p.hidden / 32;
+    return kOffFixedEnd + 3 * Round128(4 * size_t(p.dim)) + Round128(4 * size_t(DigitStride(nb_dim))) +
+           Round128(4 * size_t(nb_dim)) + Round128(4 * size_t(p.hidden)) + Round128(4 * size_t(DigitStride(nj))) +
+           Round128(4 * size_t(nj)) + Round128(sizeof(Chunk) * size_t(p.list_cap)) +
+           size_t(kMkStages) * p.stage_bytes;
 }
 
 std::string MegaFits(const MegaParams& p, size_t smem, int sm_count) {

@@ -2,30 +2,34 @@
 // n_layers x transformer layer, final RMSNorm, lm_head, greedy arg-max) in one
 // cooperative launch, for n_steps tokens in a row.
 //
-// Grid: one CTA per SM, all co-resident (cooperative launch).  Each CTA has
-// eight consumer warps and one producer warp.  The work of a step is a fixed
-// schedule of items per CTA:
+// Grid: one CTA per SM, all co-resident (cooperative launch), eight warps a
+// CTA.  The work of a step is a fixed schedule of items per CTA:
 //   QKV(l)   16-row tiles of [wq; wk; wv]          input x      -> qkv (+bias)
 //   ATTO(l)  one query head: RoPE, KV write, attention over 0..pos, then the
 //            head's 64 outputs times its block columns of wo, accumulated into
 //            x_mid with red.add (x_mid starts as x)
-//   FFN(l)   one block of 32 hidden units: its 32 gate and 32 up rows, SwiGLU,
-//            then its block column of w_down accumulated into the next x
+//   FFN-A(l) 16-row tiles of gate and up (the same rows of both), SwiGLU -> ff
+//   FFN-B(l) an equal share of the w_down chunks (row-tile major), its rows'
+//            partial sums accumulated into the next x with red.add (x starts
+//            at zero; the share that starts a row tile adds x_mid)
 //   LM       16-row tiles of lm_head -> logits; per-CTA arg-max; the last CTA
 //            to finish picks the token and releases the next step
-// Phases are ordered by global counters (release by red.add after a fence,
-// acquire by polling); weights never depend on data, so the producer warp
-// streams the CTA's whole schedule (bulk copies into a ring of mbarrier-
-// guarded stages) as far ahead as the ring allows, across phases and steps.
+// Phases (kMkPhases a layer) are ordered by global counters (release by an atomic add after a
+// fence, acquire by polling).  Weights never depend on data, so each CTA
+// streams its whole schedule (bulk copies into a ring of mbarrier-guarded
+// stages) as far ahead as the ring allows, across phases and steps: thread 0
+// refills a stage with the chunk kMkStages further on as soon as the CTA has
+// released it.  (Without a separate copy warp each thread may hold up to 255
+// registers; with nine warps an SM sub-partition would cap it at 168.)
 //
-// All weights are in the R16 layout (row tiles, qmma.cuh); wo and w_down in
-// its column-major variant R16C so a block column is contiguous.  Products are
+// All weights are in the R16 layout (row tiles, qmma.cuh); wo in its
+// column-major variant R16C so a head's block columns are contiguous.  Products are
 // the exact integer block sums of qmma.cuh (mma.m16n8k32.s8 on int8 digit
 // planes of the activations).
 //
 // Every wait is bounded: a wait that expires, or sees another CTA's abort,
-// sets the status word and the CTA leaves its step loop; the producer then
-// drains the copies it issued before the CTA exits.
+// sets the status word and the CTA leaves its step loop; thread 0 then
+// drains the copies still in flight before the CTA exits.
 #pragma once
 
 #include <string>
@@ -35,10 +39,11 @@
 namespace mlb {
 
 constexpr int kMkConsumerWarps = 8;
-constexpr int kMkThreads = (kMkConsumerWarps + 1) * 32;
-constexpr int kMkStages = 6;
+constexpr int kMkThreads = kMkConsumerWarps * 32;
+constexpr int kMkStages = 4;
+constexpr int kMkPhases = 4;        // counters per layer: QKV, attention, FFN-A, FFN-B
 constexpr int kMkAttnChunk = 256;   // positions per attention pass (one per consumer thread)
-constexpr int kMkTraceEvents = 12;  // timeline stamps per (step, layer, CTA)
+constexpr int kMkTraceEvents = 16;  // timeline stamps per (step, layer, CTA)
 
 struct MegaLayer {
     const uint8_t* wqkv[3];  // R16 wq, wk, wv
@@ -48,7 +53,7 @@ struct MegaLayer {
     const uint8_t* wo;    // R16C [dim, qd]
     const uint8_t* gate;  // R16 [hidden, dim]
     const uint8_t* up;    // R16 [hidden, dim]
-    const uint8_t* down;  // R16C [dim, hidden]
+    const uint8_t* down;  // R16 [dim, hidden]
 };
 
 struct MegaParams {
@@ -67,10 +72,11 @@ struct MegaParams {
     float* xbuf[2];
     float* xmid;
     float* qkv;
+    float* ff;  // [hidden] SwiGLU output (FFN-A -> FFN-B)
     float* logits;
     float* am_val;
     int* am_idx;
-    unsigned* counters;  // [3 * n_layers + 2] zeroed before the launch
+    unsigned* counters;  // [kMkPhases * n_layers + 2] zeroed before the launch
     int* hist;           // token history [max_seq + 1]
     int start_pos;
     int n_steps;
@@ -78,17 +84,20 @@ struct MegaParams {
     int* next_token;
     int* status;
     int stage_bytes;
+    int list_cap;  // capacity of the per-CTA chunk list (MegaListCap)
     // optional timeline: [step][layer 0..n_layers][event][CTA] %globaltimer
     // stamps; null when off.  Events: QKV 0 wait done, 11 input normalised,
     // 10 products stored, 1 signalled; attention 2 wait done, 8 softmax.V
-    // done, 9 O-projection issued, 3 signalled; FFN 4 wait done, 7 input
-    // normalised, 6 down-projection issued, 5 signalled; layer n_layers
-    // (lm_head) 0 wait done, 1 ticket taken.
+    // done, 9 O-projection flushed, 3 signalled; FFN-A 4 wait done, 7 input
+    // normalised, 5 signalled; FFN-B 12 wait done, 6 pieces done, 13
+    // signalled; layer n_layers (lm_head) 0 wait done, 1 ticket taken.
     unsigned long long* trace;
     size_t trace_cap;
 };
 
-// Dynamic shared memory of the kernel (depends on dim and stage_bytes).
+// Upper bound of the chunks one CTA of a grid of G streams per step.
+int MegaListCap(const MegaParams& p, int G);
+// Dynamic shared memory of the kernel (depends on dim, stage_bytes, list_cap).
 size_t MegaSmemBytes(const MegaParams& p);
 // Raises the kernel's shared-memory limit to smem; empty when one CTA of it
 // fits on every one of the sm_count SMs (a cooperative grid), else the reason.
