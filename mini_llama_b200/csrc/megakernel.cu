@@ -45,8 +45,8 @@ constexpr size_t kOffFlags = kOffFull + Round128(8 * kMkStages);          // 8 i
 constexpr size_t kOffScratch = kOffFlags + 128;                           // 32 floats
 constexpr size_t kOffVsx = kOffScratch + 128;                             // 4 floats
 constexpr size_t kOffVdig = kOffVsx + 128;                                // 4 planes of 4 blocks
-constexpr size_t kOffRed = kOffVdig + Round128(4 * (4 * 32 + 16));        // 8 warps x 32
-constexpr size_t kOffVec = kOffRed + 4 * 8 * 32;                          // 512 floats
+constexpr size_t kOffRed = kOffVdig + Round128(4 * (4 * 32 + 16));        // 2 x 8 warps x 32
+constexpr size_t kOffVec = kOffRed + 2 * 4 * 8 * 32;                      // 512 floats
 constexpr size_t kOffAtt = kOffVec + 4 * 512;                             // 8 warps x 128
 constexpr size_t kOffSc = kOffAtt + 4 * 8 * 128;                          // kMkAttnChunk floats
 constexpr size_t kOffFixedEnd = kOffSc + Round128(4 * kMkAttnChunk);
@@ -61,7 +61,7 @@ struct MkSmem {  // flags[0] is the CTA's abort flag (read by the producer warp 
     float* sx;      // [nb_dim] block scales of xs
     int8_t* vdig;   // 4 digit planes of a short vector (o of a head or ff of a block)
     float* vsx;     // [4] its block scales
-    float* red;     // [8 warps][32 rows]
+    float* red;     // [2][8 warps][32 rows], alternating by chunk (RedBuf)
     float* vec;     // [4 * 128] small vectors (g, u / q, k, v, o)
     float* att;     // [8 warps][hd] attention partials
     float* sc;      // [kMkAttnChunk] scores / weights of a chunk of positions
@@ -124,14 +124,16 @@ __device__ __forceinline__ bool WaitCounter(const MegaParams& p, const MkSmem& s
 }
 
 // Publishes this CTA's writes of the phase and increments the counter: the
-// barrier orders every consumer thread's writes before thread 0's fence, which
-// is cumulative over them, then the increment.
+// barrier orders every thread's writes before thread 0's release add, whose
+// release semantics are cumulative over them (no separate fence, no return
+// value to wait for).
+__device__ __forceinline__ void RedRelease(unsigned* ctr) {
+    asm volatile("red.release.gpu.global.add.u32 [%0], 1;" ::"l"(ctr) : "memory");
+}
+
 __device__ __forceinline__ void Signal(const MegaParams& p, int ctr) {
     ConsumerBar();
-    if (threadIdx.x == 0) {
-        __threadfence();
-        atomicAdd(p.counters + ctr, 1u);
-    }
+    if (threadIdx.x == 0) RedRelease(p.counters + ctr);
 }
 
 // Waits (every thread) for the stage of chunk rg.n; bounded, and it gives up
@@ -473,19 +475,24 @@ __device__ __forceinline__ void RowTilesDotImpl(const int8_t* dig, const float* 
     }
 }
 
-__device__ __forceinline__ void RowTilesDot(const MkSmem& s, const LaneMma& L, const uint8_t* stage, int ntile,
-                                            int nb, int dstride) {
-    if (ntile == 2) RowTilesDotImpl<2>(s.dig, s.sx, s.red, L, stage, nb, dstride);
-    else RowTilesDotImpl<1>(s.dig, s.sx, s.red, L, stage, nb, dstride);
+__device__ __forceinline__ void RowTilesDot(const MkSmem& s, float* red, const LaneMma& L, const uint8_t* stage,
+                                            int ntile, int nb, int dstride) {
+    if (ntile == 2) RowTilesDotImpl<2>(s.dig, s.sx, red, L, stage, nb, dstride);
+    else RowTilesDotImpl<1>(s.dig, s.sx, red, L, stage, nb, dstride);
 }
 
 // Sum of the partials of row r of tile `tile` (after a barrier).
-__device__ __forceinline__ float RowTotal(const MkSmem& s, int ntile, int tile, int r) {
+__device__ __forceinline__ float RowTotal(const float* red, int ntile, int tile, int r) {
     const int wpt = kMkConsumerWarps / ntile;
     float v = 0.0f;
-    for (int w = tile * wpt; w < (tile + 1) * wpt; ++w) v += s.red[w * 32 + tile * 16 + r];
+    for (int w = tile * wpt; w < (tile + 1) * wpt; ++w) v += red[w * 32 + tile * 16 + r];
     return v;
 }
+
+// The partial-sum buffer of chunk n: two alternate, so the chunk after next
+// is the first to overwrite one, and the release barrier of the chunk in
+// between orders the reads of the totals before it.
+__device__ __forceinline__ float* RedBuf(const MkSmem& s, const Ring& rg) { return s.red + (rg.n & 1) * 256; }
 
 // A block column (ntiles chunks of 16 rows x 32 inputs) times one block of
 // digits (scale *sxb), added into acc[row] in shared memory (each row has one
@@ -567,6 +574,14 @@ __device__ __forceinline__ void DigitsWarp(float v, int8_t* dblk, int dstride, f
 // repeats it); thread 0 issues it into the ring, the consumers consume it, in
 // the same order.
 
+// CTAs per attention head: one per wo block column when every head can have
+// that many, so each CTA of a head runs the head's attention and projects
+// through its own column; else one CTA per head and all its columns.
+__host__ __device__ __forceinline__ int HeadSplit(const MegaParams& p, int G) {
+    const int bph = p.hd / 32;
+    return p.n_heads * bph <= G ? bph : 1;
+}
+
 // FFN-B share of CTA c: the row-major chunk indices [q0, q1) of the R16 down
 // weight (ceil(dim/16) row tiles x hidden/32 blocks), equal to within one
 // chunk for every CTA, visited as pieces (row tile t, blocks b .. b+len-1)
@@ -597,6 +612,7 @@ __device__ void ForEachChunk(const MegaParams& p, int c, int G, F&& f) {
     const int t_h = p.hidden / 16;
     const int t_lm = (p.vocab + 15) / 16;
     const int bph = p.hd / 32;  // wo block columns per head
+    const int hsplit = HeadSplit(p, G);
     for (int l = 0; l < p.n_layers; ++l) {
         const MegaLayer& L = p.layers[l];
         for (int t = c; t < t_qkv; t += G) {
@@ -604,9 +620,9 @@ __device__ void ForEachChunk(const MegaParams& p, int c, int G, F&& f) {
             const int ti = seg == 0 ? t : (seg == 1 ? t - tq : t - tq - tk);
             f(Chunk{L.wqkv[seg] + size_t(ti) * tile_b, nullptr, tile_b, 0});
         }
-        for (int h = G - 1 - c; h < p.n_heads; h += G)
-            for (int j = 0; j < bph; ++j)
-                f(Chunk{L.wo + size_t(h * bph + j) * col_b, nullptr, col_b, 0});
+        for (int it = G - 1 - c; it < p.n_heads * hsplit; it += G)  // attention items (head, its wo columns)
+            for (int j = (it % hsplit) * (bph / hsplit); j < (it % hsplit + 1) * (bph / hsplit); ++j)
+                f(Chunk{L.wo + size_t((it / hsplit) * bph + j) * col_b, nullptr, col_b, 0});
         // FFN-A: gate row tile t and up row tile t in one stage
         for (int t = c; t < t_h; t += G)
             f(Chunk{L.gate + size_t(t) * tile_b, L.up + size_t(t) * tile_b, tile_b, tile_b});
@@ -644,7 +660,8 @@ __device__ unsigned Consumers(const MegaParams& p, const MkSmem& s) {
     const bool has_down = dq1 > dq0;
     const int nneed = min(dq1 - dq0, nj);
     const int fdstride = DigitStride(nj);
-    const unsigned w_qkv = WorkerCount(G, t_qkv), w_att = p.n_heads, w_ffa = WorkerCount(G, t_h),
+    const int hsplit = HeadSplit(p, G);
+    const unsigned w_qkv = WorkerCount(G, t_qkv), w_att = p.n_heads * hsplit, w_ffa = WorkerCount(G, t_h),
                    w_ffb = static_cast<unsigned>(min(static_cast<long long>(G), dQ)), w_lm = G;
     const int ctr_lm_ticket = kMkPhases * p.n_layers, ctr_token = kMkPhases * p.n_layers + 1;
     Ring rg;  // the chunk sequence thread 0 issued in the prologue, continued here
@@ -704,44 +721,55 @@ __device__ unsigned Consumers(const MegaParams& p, const MkSmem& s) {
                     const int ti = seg == 0 ? t : (seg == 1 ? t - tq : t - tq - tk);
                     const int rows = seg == 0 ? p.qd : p.kd;
                     const int off = seg == 0 ? 0 : (seg == 1 ? p.qd : p.qd + p.kd);
+                    float* red = RedBuf(s, rg);
                     WaitChunk(p, s, rg);
-                    RowTilesDot(s, L, StagePtr(p, s, rg), 1, nb_dim, dstride);
-                    ReleaseChunk(p, s, rg);
+                    RowTilesDot(s, red, L, StagePtr(p, s, rg), 1, nb_dim, dstride);
+                    ReleaseChunk(p, s, rg);  // its barrier publishes red
                     if (tid < 16) {
                         const int r = ti * 16 + tid;
                         if (r < rows) {
-                            float v = RowTotal(s, 1, 0, tid);
+                            float v = RowTotal(red, 1, 0, tid);
                             if (Lw.bias[seg]) v += i < 32 ? s.vec[16 * i + tid] : Lw.bias[seg][r];
                             p.qkv[off + r] = v;
                         }
                     }
-                    ConsumerBar();
                 }
                 Trace(p, step, l, 10);
                 Signal(p, kMkPhases * l + 0);
                 Trace(p, step, l, 1);
             }
             // ---------------- attention + O projection, one query head
-            for (int h = G - 1 - c; h < p.n_heads; h += G) {
+            for (int it = G - 1 - c; it < p.n_heads * hsplit; it += G) {
+                const int h = it / hsplit, j0 = (it % hsplit) * (bph / hsplit), j1 = j0 + bph / hsplit;
                 const int hd = p.hd, half = hd / 2, kvh = h / p.group;
                 const size_t pstride = size_t(p.n_kv) * hd;
                 const size_t lbase = size_t(l) * p.max_seq * pstride + size_t(kvh) * hd;
                 const int lpr = hd / 4, rpi = 32 / lpr;  // float4 lanes per K/V row, rows per warp pass
-                // While QKV runs: the K row of cached position tid (first chunk)
-                // into registers (its first 64 floats), and every V row plus
-                // the K rows of later chunks into L2.  None depend on this step.
-                float4 kpre[16];
+                const int rsub = lane / lpr, col = lane % lpr;
+                // While QKV runs, the cached positions of the first chunk into
+                // registers: the K row of position tid (its first 32 floats),
+                // and this warp's V row pieces for the values pass (rows
+                // 32 warp + i rpi + rsub, float4 column col); K and V rows of
+                // later chunks into L2.  None depend on this step.
+                float4 kpre[8], vpre0[16];
                 {
                     const bool kp = tid < pos;
                     const float4* kr = reinterpret_cast<const float4*>(p.kc + lbase + size_t(kp ? tid : 0) * pstride);
 #pragma unroll
-                    for (int i = 0; i < 16; ++i)
+                    for (int i = 0; i < 8; ++i)
                         kpre[i] = kp && i < lpr ? __ldcg(kr + i) : make_float4(0.f, 0.f, 0.f, 0.f);
+#pragma unroll
+                    for (int i = 0; i < 16; ++i) {
+                        const int r = warp * 32 + i * rpi + rsub;
+                        vpre0[i] = i < lpr && r < pos
+                                       ? __ldcg(reinterpret_cast<const float4*>(p.vc + lbase + size_t(r) * pstride) + col)
+                                       : make_float4(0.f, 0.f, 0.f, 0.f);
+                    }
                 }
-                for (int pp = tid; pp < pos; pp += 256)
-                    BulkPrefetchL2(p.vc + lbase + size_t(pp) * pstride, static_cast<uint32_t>(hd) * 4);
-                for (int pp = kMkAttnChunk + tid; pp < pos; pp += 256)
+                for (int pp = kMkAttnChunk + tid; pp < pos; pp += 256) {
                     BulkPrefetchL2(p.kc + lbase + size_t(pp) * pstride, static_cast<uint32_t>(hd) * 4);
+                    BulkPrefetchL2(p.vc + lbase + size_t(pp) * pstride, static_cast<uint32_t>(hd) * 4);
+                }
                 // RoPE rows of this position (s.att is free until the values pass)
                 float* ct = s.att;
                 float* st = s.att + half;
@@ -772,7 +800,7 @@ __device__ unsigned Consumers(const MegaParams& p, const MkSmem& s) {
                     kn[b2] = __fadd_rn(__fmul_rn(x0, sn), __fmul_rn(x1, cs));
                 }
                 ConsumerBar();
-                if (h % p.group == 0)  // the group's first head stores this token's k, v
+                if (h % p.group == 0 && j0 == 0)  // one CTA of the group's first head stores k, v
                     for (int i = tid; i < hd; i += 256) {
                         p.kc[lbase + size_t(pos) * pstride + i] = kn[i];
                         p.vc[lbase + size_t(pos) * pstride + i] = vn[i];
@@ -781,7 +809,6 @@ __device__ unsigned Consumers(const MegaParams& p, const MkSmem& s) {
                 // Scores: a thread per position (its K row as float4 loads, all
                 // in flight together).  Values: a warp per 32 positions, lanes
                 // over (row, float4 column), every row load in flight together.
-                const int rsub = lane / lpr, col = lane % lpr;
                 float m_run = -INFINITY, l_run = 0.0f;
                 for (int base = 0; base <= pos; base += kMkAttnChunk) {
                     const int pp = base + tid;
@@ -803,7 +830,7 @@ __device__ unsigned Consumers(const MegaParams& p, const MkSmem& s) {
                             int i0 = 0;
                             if (base == 0) {  // the prefetched part of the row
 #pragma unroll
-                                for (int i = 0; i < 16; ++i)
+                                for (int i = 0; i < 8; ++i)
                                     if (i < lpr) {
                                         const float4 qv = q4[i];
                                         dot = fmaf(qv.x, kpre[i].x, dot);
@@ -811,7 +838,7 @@ __device__ unsigned Consumers(const MegaParams& p, const MkSmem& s) {
                                         dot = fmaf(qv.z, kpre[i].z, dot);
                                         dot = fmaf(qv.w, kpre[i].w, dot);
                                     }
-                                i0 = 16;
+                                i0 = 8;
                             }
                             for (; i0 < lpr; i0 += 8) {  // 8 loads in flight
                                 float4 kv[8];
@@ -831,18 +858,23 @@ __device__ unsigned Consumers(const MegaParams& p, const MkSmem& s) {
                         }
                         sc = dot * p.scale;
                     }
-                    // this warp's first 16 V row pieces, loaded before the
-                    // softmax reductions so their latency overlaps them
+                    // this warp's first 16 V row pieces: the prefetched ones in
+                    // the first chunk (later chunks load them here, before the
+                    // softmax reductions so their latency overlaps them); the
+                    // current position's row comes from shared memory
                     const int r0 = base + warp * 32;
                     float4 vpre[16];
 #pragma unroll
                     for (int i = 0; i < 16; ++i) {
                         const int r = r0 + i * rpi + rsub;
-                        vpre[i] = make_float4(0.f, 0.f, 0.f, 0.f);
-                        if (i < lpr && r < pos)
-                            vpre[i] = __ldcg(reinterpret_cast<const float4*>(p.vc + lbase + size_t(r) * pstride) + col);
-                        else if (i < lpr && r == pos)
-                            vpre[i] = reinterpret_cast<const float4*>(vn)[col];
+                        if (base == 0) {
+                            vpre[i] = vpre0[i];
+                        } else {
+                            vpre[i] = make_float4(0.f, 0.f, 0.f, 0.f);
+                            if (i < lpr && r < pos)
+                                vpre[i] = __ldcg(reinterpret_cast<const float4*>(p.vc + lbase + size_t(r) * pstride) + col);
+                        }
+                        if (i < lpr && r == pos) vpre[i] = reinterpret_cast<const float4*>(vn)[col];
                     }
                     const float mc = ConsumerMax(sc, s.scratch);
                     const float mnew = fmaxf(m_run, mc);
@@ -910,8 +942,8 @@ __device__ unsigned Consumers(const MegaParams& p, const MkSmem& s) {
                     DigitsWarp(o[d] / l_run, s.vdig + (d >> 5) * 32, vstride, s.vsx + (d >> 5));
                 ConsumerBar();
                 Trace(p, step, l, 8);
-                // wo block columns of the head into acc, then one red.add pass
-                for (int j = 0; j < bph; ++j) {
+                // this item's wo block columns into acc, then one red.add pass
+                for (int j = j0; j < j1; ++j) {
                     WaitChunk(p, s, rg);
                     ColumnDotSmem(L, StagePtr(p, s, rg), ntiles_dim, p.dim,
                                   s.vdig + j * 32, vstride, s.vsx + j, s.acc);
@@ -933,15 +965,15 @@ __device__ unsigned Consumers(const MegaParams& p, const MkSmem& s) {
                 RmsNormDigits(s.xs, s.nw, p.dim, p.eps, s.dig, dstride, s.sx, s.scratch);
                 Trace(p, step, l, 7);
                 for (int t = c; t < t_h; t += G) {
+                    float* red = RedBuf(s, rg);
                     WaitChunk(p, s, rg);
-                    RowTilesDot(s, L, StagePtr(p, s, rg), 2, nb_dim, dstride);
-                    ReleaseChunk(p, s, rg);  // its barrier publishes s.red
+                    RowTilesDot(s, red, L, StagePtr(p, s, rg), 2, nb_dim, dstride);
+                    ReleaseChunk(p, s, rg);  // its barrier publishes red
                     if (tid < 16) {
-                        const float g = RowTotal(s, 2, 0, tid), u = RowTotal(s, 2, 1, tid);
+                        const float g = RowTotal(red, 2, 0, tid), u = RowTotal(red, 2, 1, tid);
                         const float sig = 1.0f / (1.0f + expf(-g));
                         p.ff[t * 16 + tid] = g * sig * u;
                     }
-                    ConsumerBar();
                 }
                 Signal(p, kMkPhases * l + 2);
                 Trace(p, step, l, 5);
@@ -961,17 +993,16 @@ __device__ unsigned Consumers(const MegaParams& p, const MkSmem& s) {
                 int t_first = -1, t_last = -1;
                 bool res_first = false;
                 ForEachDownPiece(p, c, G, [&](int t, int b, int len) {
+                    float* red = RedBuf(s, rg);
                     WaitChunk(p, s, rg);
-                    RowTilesDotImpl<1>(s.fdig + b * 32, s.fsx + b, s.red, L,
-                                       StagePtr(p, s, rg), len, fdstride);
-                    ReleaseChunk(p, s, rg);  // its barrier publishes s.red
+                    RowTilesDotImpl<1>(s.fdig + b * 32, s.fsx + b, red, L, StagePtr(p, s, rg), len, fdstride);
+                    ReleaseChunk(p, s, rg);  // its barrier publishes red
                     if (t_first < 0) {
                         t_first = t;
                         res_first = b == 0;
                     }
                     t_last = t;
-                    if (tid < 16) s.acc[t * 16 + tid] += RowTotal(s, 1, 0, tid);
-                    ConsumerBar();
+                    if (tid < 16) s.acc[t * 16 + tid] += RowTotal(red, 1, 0, tid);
                 });
                 Trace(p, step, l, 6);
                 // the CTA whose share starts a row tile at block 0 adds x_mid
@@ -1002,13 +1033,14 @@ __device__ unsigned Consumers(const MegaParams& p, const MkSmem& s) {
         for (int t2 = c; 2 * t2 < t_lm; t2 += G) {
             // a lone last tile leaves stale bytes in the stage's second half;
             // its rows are past the vocabulary and skipped
+            float* red = RedBuf(s, rg);
             WaitChunk(p, s, rg);
-            RowTilesDot(s, L, StagePtr(p, s, rg), 2, nb_dim, dstride);
-            ReleaseChunk(p, s, rg);
+            RowTilesDot(s, red, L, StagePtr(p, s, rg), 2, nb_dim, dstride);
+            ReleaseChunk(p, s, rg);  // its barrier publishes red
             if (tid < 32) {
                 const int r = (2 * t2 + (tid >> 4)) * 16 + (tid & 15);
                 if (r < p.vocab) {
-                    const float v = RowTotal(s, 2, tid >> 4, tid & 15);
+                    const float v = RowTotal(red, 2, tid >> 4, tid & 15);
                     p.logits[r] = v;
                     if (v > best || (v == best && r < besti)) {
                         best = v;
@@ -1016,7 +1048,6 @@ __device__ unsigned Consumers(const MegaParams& p, const MkSmem& s) {
                     }
                 }
             }
-            ConsumerBar();
         }
         // CTA arg-max (first maximum) over the 32 candidate threads
         if (warp == 0) {
@@ -1065,8 +1096,7 @@ __device__ unsigned Consumers(const MegaParams& p, const MkSmem& s) {
                 const int tok = bi == 0x7fffffff ? 0 : bi;
                 if (pos + 1 >= p.gen_from && pos + 1 <= p.max_seq) p.hist[pos + 1] = tok;
                 *p.next_token = tok;
-                __threadfence();
-                atomicAdd(p.counters + ctr_token, 1u);
+                RedRelease(p.counters + ctr_token);
             }
         }
         ConsumerBar();
@@ -1152,7 +1182,8 @@ int MegaListCap(const MegaParams& p, int G) {
     const int share = static_cast<int>((dQ + G - 1) / G);  // down chunks of one CTA at most
     const int smax = p.stage_bytes / kR16Chunk;
     const int pieces = share / min(smax, p.hidden / 32) + 2;  // + the splits at row-tile ends
-    return p.n_layers * (per(t_qkv) + per(p.n_heads) * (p.hd / 32) + per(p.hidden / 16) + pieces) +
+    const int hsplit = HeadSplit(p, G);
+    return p.n_layers * (per(t_qkv) + per(p.n_heads * hsplit) * (p.hd / 32 / hsplit) + per(p.hidden / 16) + pieces) +
            per((t_lm + 1) / 2);
 }
 
