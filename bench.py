@@ -125,6 +125,23 @@ def reference_sample(threads: int, steps: int, warmup: int, prompt_len=8, n_pred
     return statistics.mean(vals) if vals else None, timed
 
 
+def max_over_ranks(dist, value: float, device: str) -> float:
+    """The largest value over all ranks (every rank calls it, in the same
+    order); the value itself with a single process (dist None)."""
+    if dist is None:
+        return value
+    import torch
+    t = torch.tensor([value], dtype=torch.float64, device=device)
+    dist.all_reduce(t, op=dist.ReduceOp.MAX)
+    return float(t.item())
+
+
+def job_throughput(world: int, tokens_per_rank_step: int, steps: int, secs: float) -> float:
+    """Whole-job tokens/s: every rank decodes its own sequence (replicas), the
+    job takes the slowest rank's time."""
+    return world * tokens_per_rank_step * steps / secs
+
+
 def run_reference(args):
     rank = int(os.environ.get("RANK", "0"))
     if rank != 0:
@@ -254,12 +271,8 @@ def run_ours(args):
     e1.synchronize()
     barrier()
     clk = clocks.stop()
-    secs = e0.elapsed_time(e1) / 1e3
-    if dist is not None:
-        t = torch.tensor([secs], device=f"cuda:{dev}")
-        dist.all_reduce(t, op=dist.ReduceOp.MAX)
-        secs = float(t.item())
-    value = world * new * args.steps / secs
+    secs = max_over_ranks(dist, e0.elapsed_time(e1) / 1e3, f"cuda:{dev}")
+    value = job_throughput(world, new, args.steps, secs)
 
     # e2e: host start token in, host token ids out, through mlb_session_generate
     start = torch.empty(1, dtype=torch.int32, pin_memory=True)
@@ -279,12 +292,8 @@ def run_ours(args):
         for _ in range(args.steps):
             e2e_step()
         barrier()
-        e2e_secs = time.perf_counter() - t0
-        if dist is not None:
-            t = torch.tensor([e2e_secs], device=f"cuda:{dev}")
-            dist.all_reduce(t, op=dist.ReduceOp.MAX)
-            e2e_secs = float(t.item())
-        e2e = world * NEW * args.steps / e2e_secs
+        e2e_secs = max_over_ranks(dist, time.perf_counter() - t0, f"cuda:{dev}")
+        e2e = job_throughput(world, NEW, args.steps, e2e_secs)
 
     peaks = measured_peaks()
     step_bytes = sum(algorithmic_bytes_per_token(p) for p in range(PROMPT, PROMPT + new))

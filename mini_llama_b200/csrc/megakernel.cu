@@ -198,50 +198,6 @@ __device__ __forceinline__ int RoundSmall(float v) {
     return __float_as_int(v + 12582912.0f) - 0x4B400000;
 }
 
-// Digit planes and scales of the count blocks (start + i) mod nb of x (in
-// shared memory, block b at x + 32 b), stored at block b of dig / sx: eight
-// threads per block, four elements each (the block max by three shuffles).
-__device__ __forceinline__ void DigitsBlocks(const float* x, int start, int count, int nb, int8_t* dig,
-                                          int dstride, float* sx) {
-    for (int k0 = 0; k0 < count * 8; k0 += 256) {  // count * 8 threads, groups of 8 share a trip
-        const int k = k0 + threadIdx.x;
-        const bool on = k < count * 8;
-        const int b = on ? (start + k / 8) % nb : 0, e = 4 * (k % 8);
-        float4 v = make_float4(0.f, 0.f, 0.f, 0.f);
-        if (on) v = *reinterpret_cast<const float4*>(x + b * 32 + e);
-        float mx = fmaxf(fmaxf(fabsf(v.x), fabsf(v.y)), fmaxf(fabsf(v.z), fabsf(v.w)));
-        mx = fmaxf(mx, __shfl_xor_sync(0xffffffffu, mx, 1));
-        mx = fmaxf(mx, __shfl_xor_sync(0xffffffffu, mx, 2));
-        mx = fmaxf(mx, __shfl_xor_sync(0xffffffffu, mx, 4));
-        if (!on) continue;
-        const int ex = static_cast<int>((__float_as_uint(mx) >> 23) & 0xff) - 126;
-        const float y[4] = {v.x, v.y, v.z, v.w};
-        uint32_t p2 = 0, p1 = 0, p0 = 0;
-        float sc = 0.0f;
-        if (mx > 0.0f && ex >= -104) {
-            const float up = __uint_as_float(static_cast<uint32_t>(127 + 22 - ex) << 23);
-            sc = __uint_as_float(static_cast<uint32_t>(127 + ex - 22) << 23);
-#pragma unroll
-            for (int j = 0; j < 4; ++j) {
-                const int xi = RoundSmall(y[j] * up);
-                const int d0 = (xi << 24) >> 24;
-                const int x1 = (xi - d0) >> 8;
-                const int d1 = (x1 << 24) >> 24;
-                const int d2 = (x1 - d1) >> 8;
-                p2 |= (static_cast<uint32_t>(d2) & 0xffu) << (8 * j);
-                p1 |= (static_cast<uint32_t>(d1) & 0xffu) << (8 * j);
-                p0 |= (static_cast<uint32_t>(d0) & 0xffu) << (8 * j);
-            }
-        }
-        uint32_t* base = reinterpret_cast<uint32_t*>(dig + b * 32 + e);
-        base[0] = p2;
-        base[dstride / 4] = p1;
-        base[2 * (dstride / 4)] = p0;
-        base[3 * (dstride / 4)] = 0u;
-        if ((k & 7) == 0) sx[b] = sc;
-    }
-    ConsumerBar();
-}
 
 __device__ float ConsumerMax(float v, float* scratch) {
     v = WarpMax(v);
@@ -260,61 +216,117 @@ __device__ float ConsumerMax(float v, float* scratch) {
 // per four elements, eight threads per 32-block (the block max by three
 // shuffles).  Each normalised value is x * rsqrt(mean(x^2) + eps) * w in the
 // reference's product order.
+__device__ __forceinline__ float4 LdsF32x4(uint32_t a) {
+    float4 v;
+    asm volatile("ld.shared.v4.f32 {%0, %1, %2, %3}, [%4];" : "=f"(v.x), "=f"(v.y), "=f"(v.z), "=f"(v.w) : "r"(a));
+    return v;
+}
+
+__device__ __forceinline__ void StsU32(uint32_t a, uint32_t v) {
+    asm volatile("st.shared.u32 [%0], %1;" ::"r"(a), "r"(v) : "memory");
+}
+
+// Digits of four elements y[0..3] of a 32-block whose eight holders are the
+// aligned eight lanes of this thread (block max by three shuffles; every lane
+// takes part); when `on`, the four digit bytes of each plane go to dq +
+// plane * dstride.  Returns the block scale.
+__device__ __forceinline__ float QuadDigits(const float (&y)[4], bool on, uint32_t dq, int dstride) {
+    float mx = fmaxf(fmaxf(fabsf(y[0]), fabsf(y[1])), fmaxf(fabsf(y[2]), fabsf(y[3])));
+    mx = fmaxf(mx, __shfl_xor_sync(0xffffffffu, mx, 1));
+    mx = fmaxf(mx, __shfl_xor_sync(0xffffffffu, mx, 2));
+    mx = fmaxf(mx, __shfl_xor_sync(0xffffffffu, mx, 4));
+    const int e = static_cast<int>((__float_as_uint(mx) >> 23) & 0xff) - 126;
+    uint32_t p2 = 0, p1 = 0, p0 = 0;
+    float sc = 0.0f;
+    if (mx > 0.0f && e >= -104) {
+        const float up = __uint_as_float(static_cast<uint32_t>(127 + 22 - e) << 23);
+        sc = __uint_as_float(static_cast<uint32_t>(127 + e - 22) << 23);
+#pragma unroll
+        for (int k = 0; k < 4; ++k) {
+            const int xi = RoundSmall(y[k] * up);
+            const int d0 = (xi << 24) >> 24;
+            const int x1 = (xi - d0) >> 8;
+            const int d1 = (x1 << 24) >> 24;
+            const int d2 = (x1 - d1) >> 8;
+            p2 |= (static_cast<uint32_t>(d2) & 0xffu) << (8 * k);
+            p1 |= (static_cast<uint32_t>(d1) & 0xffu) << (8 * k);
+            p0 |= (static_cast<uint32_t>(d0) & 0xffu) << (8 * k);
+        }
+    }
+    if (on) {
+        StsU32(dq, p2);
+        StsU32(dq + dstride, p1);
+        StsU32(dq + 2 * dstride, p0);
+        StsU32(dq + 3 * dstride, 0u);
+    }
+    return sc;
+}
+
+// RMSNorm of x (n % 32 == 0, shared memory) straight into the digit planes
+// and block scales of the normalised vector, which is not stored: a thread
+// per four elements, eight threads per 32-block.  Each normalised value is
+// x * rsqrt(mean(x^2) + eps) * w in the reference's product order.  Vectors of
+// up to 1024 elements stay in registers between the two passes.
 __device__ __forceinline__ void RmsNormDigits(const float* x, const float* w, int n, float eps, int8_t* dig,
-                              int dstride, float* sx, float* scratch) {
+                                              int dstride, float* sx, float* scratch) {
     const int n4 = n / 4;
+    const uint32_t xa = SmemAddr(x), wa = SmemAddr(w), da = SmemAddr(dig);
+    const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
+    float4 v0 = make_float4(0.f, 0.f, 0.f, 0.f);
+    if (tid < n4) v0 = LdsF32x4(xa + 16 * tid);
     float ss = 0.0f;
-    for (int i = threadIdx.x; i < n4; i += 256) {
-        const float4 v = reinterpret_cast<const float4*>(x)[i];
+    ss = fmaf(v0.x, v0.x, ss);
+    ss = fmaf(v0.y, v0.y, ss);
+    ss = fmaf(v0.z, v0.z, ss);
+    ss = fmaf(v0.w, v0.w, ss);
+    for (int i = tid + 256; i < n4; i += 256) {
+        const float4 v = LdsF32x4(xa + 16 * i);
         ss = fmaf(v.x, v.x, ss);
         ss = fmaf(v.y, v.y, ss);
         ss = fmaf(v.z, v.z, ss);
         ss = fmaf(v.w, v.w, ss);
     }
-    const float tot = ConsumerSum(ss, scratch);
+    // one barrier: scratch is not written again before the closing barrier
+    ss = WarpSum(ss);
+    if (lane == 0) scratch[warp] = ss;
+    ConsumerBar();
+    const float4 s0 = LdsF32x4(SmemAddr(scratch)), s1 = LdsF32x4(SmemAddr(scratch) + 16);
+    const float tot = ((s0.x + s0.y) + (s0.z + s0.w)) + ((s1.x + s1.y) + (s1.z + s1.w));
     const float scale = 1.0f / sqrtf(tot / static_cast<float>(n) + eps);
     // n4 is a multiple of 8, so the eight threads of a block share every trip
     for (int i0 = 0; i0 < n4; i0 += 256) {
-        const int i = i0 + threadIdx.x;
+        const int i = i0 + tid;
         const bool on = i < n4;
         float y[4] = {0.f, 0.f, 0.f, 0.f};
         if (on) {
-            const float4 v = reinterpret_cast<const float4*>(x)[i];
-            const float4 g = reinterpret_cast<const float4*>(w)[i];
+            const float4 v = i0 == 0 ? v0 : LdsF32x4(xa + 16 * i);
+            const float4 g = LdsF32x4(wa + 16 * i);
             y[0] = v.x * scale * g.x;
             y[1] = v.y * scale * g.y;
             y[2] = v.z * scale * g.z;
             y[3] = v.w * scale * g.w;
         }
-        float mx = fmaxf(fmaxf(fabsf(y[0]), fabsf(y[1])), fmaxf(fabsf(y[2]), fabsf(y[3])));
-        mx = fmaxf(mx, __shfl_xor_sync(0xffffffffu, mx, 1));
-        mx = fmaxf(mx, __shfl_xor_sync(0xffffffffu, mx, 2));
-        mx = fmaxf(mx, __shfl_xor_sync(0xffffffffu, mx, 4));
-        if (!on) continue;
-        const int e = static_cast<int>((__float_as_uint(mx) >> 23) & 0xff) - 126;
-        uint32_t p2 = 0, p1 = 0, p0 = 0;
-        float sc = 0.0f;
-        if (mx > 0.0f && e >= -104) {
-            const float up = __uint_as_float(static_cast<uint32_t>(127 + 22 - e) << 23);
-            sc = __uint_as_float(static_cast<uint32_t>(127 + e - 22) << 23);
-#pragma unroll
-            for (int k = 0; k < 4; ++k) {
-                const int xi = RoundSmall(y[k] * up);
-                const int d0 = (xi << 24) >> 24;
-                const int x1 = (xi - d0) >> 8;
-                const int d1 = (x1 << 24) >> 24;
-                const int d2 = (x1 - d1) >> 8;
-                p2 |= (static_cast<uint32_t>(d2) & 0xffu) << (8 * k);
-                p1 |= (static_cast<uint32_t>(d1) & 0xffu) << (8 * k);
-                p0 |= (static_cast<uint32_t>(d0) & 0xffu) << (8 * k);
-            }
-        }
-        uint32_t* base = reinterpret_cast<uint32_t*>(dig + 4 * i);
-        base[0] = p2;
-        base[dstride / 4] = p1;
-        base[2 * (dstride / 4)] = p0;
-        base[3 * (dstride / 4)] = 0u;
-        if ((threadIdx.x & 7) == 0) sx[i / 8] = sc;
+        const float sc = QuadDigits(y, on, da + 4 * i, dstride);
+        if (on && (tid & 7) == 0) sx[i / 8] = sc;
+    }
+    ConsumerBar();
+}
+
+// Digit planes and scales of the count blocks (start + i) mod nb of x (in
+// shared memory, block b at x + 32 b), stored at block b of dig / sx: eight
+// threads per block, four elements each (the block max by three shuffles).
+__device__ __forceinline__ void DigitsBlocks(const float* x, int start, int count, int nb, int8_t* dig,
+                                             int dstride, float* sx) {
+    const uint32_t xa = SmemAddr(x), da = SmemAddr(dig);
+    for (int k0 = 0; k0 < count * 8; k0 += 256) {  // count * 8 threads, groups of 8 share a trip
+        const int k = k0 + threadIdx.x;
+        const bool on = k < count * 8;
+        const int b = on ? (start + k / 8) % nb : 0, e = 4 * (k % 8);
+        float4 v = make_float4(0.f, 0.f, 0.f, 0.f);
+        if (on) v = LdsF32x4(xa + 4 * (b * 32 + e));
+        const float y[4] = {v.x, v.y, v.z, v.w};
+        const float sc = QuadDigits(y, on, da + b * 32 + e, dstride);
+        if (on && (k & 7) == 0) sx[b] = sc;
     }
     ConsumerBar();
 }
@@ -746,29 +758,22 @@ __device__ unsigned Consumers(const MegaParams& p, const MkSmem& s) {
                 const size_t lbase = size_t(l) * p.max_seq * pstride + size_t(kvh) * hd;
                 const int lpr = hd / 4, rpi = 32 / lpr;  // float4 lanes per K/V row, rows per warp pass
                 const int rsub = lane / lpr, col = lane % lpr;
-                // While QKV runs, the cached positions of the first chunk into
-                // registers: the K row of position tid (its first 32 floats),
-                // and this warp's V row pieces for the values pass (rows
-                // 32 warp + i rpi + rsub, float4 column col); K and V rows of
-                // later chunks into L2.  None depend on this step.
-                float4 kpre[8], vpre0[16];
+                // While QKV runs: the K row of cached position tid (first
+                // chunk; its first 64 floats) into registers, every cached V
+                // row and the K rows of later chunks into L2.  None depend on
+                // this step.
+                float4 kpre[16];
                 {
                     const bool kp = tid < pos;
                     const float4* kr = reinterpret_cast<const float4*>(p.kc + lbase + size_t(kp ? tid : 0) * pstride);
 #pragma unroll
-                    for (int i = 0; i < 8; ++i)
+                    for (int i = 0; i < 16; ++i)
                         kpre[i] = kp && i < lpr ? __ldcg(kr + i) : make_float4(0.f, 0.f, 0.f, 0.f);
-#pragma unroll
-                    for (int i = 0; i < 16; ++i) {
-                        const int r = warp * 32 + i * rpi + rsub;
-                        vpre0[i] = i < lpr && r < pos
-                                       ? __ldcg(reinterpret_cast<const float4*>(p.vc + lbase + size_t(r) * pstride) + col)
-                                       : make_float4(0.f, 0.f, 0.f, 0.f);
-                    }
                 }
-                for (int pp = kMkAttnChunk + tid; pp < pos; pp += 256) {
-                    BulkPrefetchL2(p.kc + lbase + size_t(pp) * pstride, static_cast<uint32_t>(hd) * 4);
+                for (int pp = tid; pp < pos; pp += 256) {
                     BulkPrefetchL2(p.vc + lbase + size_t(pp) * pstride, static_cast<uint32_t>(hd) * 4);
+                    if (pp >= kMkAttnChunk)
+                        BulkPrefetchL2(p.kc + lbase + size_t(pp) * pstride, static_cast<uint32_t>(hd) * 4);
                 }
                 // RoPE rows of this position (s.att is free until the values pass)
                 float* ct = s.att;
@@ -830,7 +835,7 @@ __device__ unsigned Consumers(const MegaParams& p, const MkSmem& s) {
                             int i0 = 0;
                             if (base == 0) {  // the prefetched part of the row
 #pragma unroll
-                                for (int i = 0; i < 8; ++i)
+                                for (int i = 0; i < 16; ++i)
                                     if (i < lpr) {
                                         const float4 qv = q4[i];
                                         dot = fmaf(qv.x, kpre[i].x, dot);
@@ -838,7 +843,7 @@ __device__ unsigned Consumers(const MegaParams& p, const MkSmem& s) {
                                         dot = fmaf(qv.z, kpre[i].z, dot);
                                         dot = fmaf(qv.w, kpre[i].w, dot);
                                     }
-                                i0 = 8;
+                                i0 = 16;
                             }
                             for (; i0 < lpr; i0 += 8) {  // 8 loads in flight
                                 float4 kv[8];
@@ -858,23 +863,19 @@ __device__ unsigned Consumers(const MegaParams& p, const MkSmem& s) {
                         }
                         sc = dot * p.scale;
                     }
-                    // this warp's first 16 V row pieces: the prefetched ones in
-                    // the first chunk (later chunks load them here, before the
-                    // softmax reductions so their latency overlaps them); the
+                    // this warp's first 16 V row pieces, loaded before the
+                    // softmax reductions so their latency overlaps them; the
                     // current position's row comes from shared memory
                     const int r0 = base + warp * 32;
                     float4 vpre[16];
 #pragma unroll
                     for (int i = 0; i < 16; ++i) {
                         const int r = r0 + i * rpi + rsub;
-                        if (base == 0) {
-                            vpre[i] = vpre0[i];
-                        } else {
-                            vpre[i] = make_float4(0.f, 0.f, 0.f, 0.f);
-                            if (i < lpr && r < pos)
-                                vpre[i] = __ldcg(reinterpret_cast<const float4*>(p.vc + lbase + size_t(r) * pstride) + col);
-                        }
-                        if (i < lpr && r == pos) vpre[i] = reinterpret_cast<const float4*>(vn)[col];
+                        vpre[i] = make_float4(0.f, 0.f, 0.f, 0.f);
+                        if (i < lpr && r < pos)
+                            vpre[i] = __ldcg(reinterpret_cast<const float4*>(p.vc + lbase + size_t(r) * pstride) + col);
+                        else if (i < lpr && r == pos)
+                            vpre[i] = reinterpret_cast<const float4*>(vn)[col];
                     }
                     const float mc = ConsumerMax(sc, s.scratch);
                     const float mnew = fmaxf(m_run, mc);
