@@ -299,9 +299,9 @@ int mlb_session_use_persistent(mlb_session* session, int enable);
  *   buffer[((step * (n_layers + 1) + layer) * 16 + event) * sm_count + cta]
  * for each CTA that takes part in the phase.  QKV: 0 wait done, 11 input
  * normalised, 10 products stored, 1 signalled.  Attention: 2 wait done,
- * 8 softmax.V done, 9 O-projection flushed, 3 signalled.  FFN gate/up: 4 wait
- * done, 7 input normalised, 5 signalled.  FFN down: 12 wait done, 6 products
- * done, 13 signalled.  Layer n_layers (lm_head): 0 wait done, 1 done.  Stamps past `entries` are dropped; the
+ * 8 softmax.V done, 9 O-projection flushed, 3 signalled.  FFN: 4 wait done,
+ * 7 input normalised, 6 down-projection flushed, 5 signalled.  Layer n_layers
+ * (lm_head): 0 wait done, 1 done.  Stamps past `entries` are dropped; the
  * buffer is not cleared.  NULL, 0 turns the timeline off. */
 int mlb_session_trace(mlb_session* session, unsigned long long* device_buffer, size_t entries);
 /* Device pointers of the session KV cache. */

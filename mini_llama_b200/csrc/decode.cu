@@ -77,8 +77,8 @@ struct mlb_model {
     size_t r16_bytes = 0;
     Slot r16_lm_head;
     std::vector<std::array<Slot, 15>> r16_layer;
-    // wo also in R16C (block columns contiguous) when the persistent decode
-    // kernel can run the model
+    // wo and w_down also in R16C (block columns contiguous) when the
+    // persistent decode kernel can run the model
     bool r16c = false;
     std::string mega_reason = "weights are not Q8_0";  // why not, when r16c is false
     std::vector<std::array<Slot, 2>> r16c_layer;
@@ -92,7 +92,7 @@ struct mlb_model {
         return static_cast<const uint8_t*>(r16) + s.offset;
     }
     const uint8_t* R16C(int l, int kind) const {
-        return static_cast<const uint8_t*>(r16) + r16c_layer[l][0].offset;
+        return static_cast<const uint8_t*>(r16) + r16c_layer[l][kind == MLB_W_WO ? 0 : 1].offset;
     }
 };
 
@@ -199,7 +199,7 @@ void RepackOne(mlb_model* m, DeviceContext& c, int l, int kind) {
     LinearShape(m->cfg, kind, rows, cols);
     const auto& src = m->Get(l, kind);
     LaunchRepackQ80R16(c, m->Ptr(src), rows, cols, const_cast<uint8_t*>(m->R16(l, kind)));
-    if (m->r16c && kind == MLB_W_WO)
+    if (m->r16c && (kind == MLB_W_WO || kind == MLB_W_DOWN))
         LaunchRepackQ80R16(c, m->Ptr(src), rows, cols, const_cast<uint8_t*>(m->R16C(l, kind)), true);
 }
 
@@ -270,7 +270,10 @@ void PrepareR16(mlb_model* m, DeviceContext& c, int chunks) {
     m->r16c = m->mega_reason.empty();
     if (m->r16c) {
         m->r16c_layer.resize(m->cfg.n_layers);
-        for (int l = 0; l < m->cfg.n_layers; ++l) m->r16c_layer[l][0] = slot(MLB_W_WO);
+        for (int l = 0; l < m->cfg.n_layers; ++l) {
+            m->r16c_layer[l][0] = slot(MLB_W_WO);
+            m->r16c_layer[l][1] = slot(MLB_W_DOWN);
+        }
     }
     m->r16_bytes = off;
     CheckCuda(cudaMallocAsync(&m->r16, off, c.stream), "cudaMallocAsync(R16 weights)");
@@ -469,7 +472,7 @@ void PrepareMega(mlb_session* s, DeviceContext& c) {
         L.wo = m->R16C(l, MLB_W_WO);
         L.gate = m->R16(l, MLB_W_GATE);
         L.up = m->R16(l, MLB_W_UP);
-        L.down = m->R16(l, MLB_W_DOWN);
+        L.down = m->R16C(l, MLB_W_DOWN);
     }
     MegaLayer* dl = static_cast<MegaLayer*>(DevAlloc(s, c, layers.size() * sizeof(MegaLayer)));
     CheckCuda(cudaMemcpyAsync(dl, layers.data(), layers.size() * sizeof(MegaLayer),
@@ -505,7 +508,6 @@ void PrepareMega(mlb_session* s, DeviceContext& c) {
     p.xbuf[1] = x2;
     p.xmid = s->xmid;
     p.qkv = s->qkv;
-    p.ff = s->ff;
     p.logits = s->logits;
     p.am_val = s->am_val;
     p.am_idx = s->am_idx;

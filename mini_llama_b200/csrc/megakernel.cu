@@ -65,10 +65,7 @@ struct MkSmem {  // flags[0] is the CTA's abort flag (read by the producer warp 
     float* vec;     // [4 * 128] small vectors (g, u / q, k, v, o)
     float* att;     // [8 warps][hd] attention partials
     float* sc;      // [kMkAttnChunk] scores / weights of a chunk of positions
-    float* acc;     // [dim] block-column / down products of the CTA, flushed by red.add
-    float* fx;      // [hidden] the ff blocks FFN-B needs
-    int8_t* fdig;   // 4 digit planes of fx, stride DigitStride(hidden / 32)
-    float* fsx;     // [hidden / 32] their block scales
+    float* acc;     // [dim] block-column products of the CTA, flushed by red.add
     float* scratch; // [32]
     int* flags;     // [0] abort, [1] token, [2] chunks per step, [4] decision, [5] chunks issued
 };
@@ -151,7 +148,8 @@ __device__ __forceinline__ uint8_t* StagePtr(const MegaParams& p, const MkSmem& 
     return s.ring + size_t(rg.n % kMkStages) * p.stage_bytes;
 }
 
-// List entry li into ring slot k % kMkStages; thread 0 only.
+// List entry li into ring slot k % kMkStages; one thread at a time (thread 0
+// in the prologue, then lane 0 of the last warp).
 __device__ __forceinline__ void IssueChunk(const MegaParams& p, const MkSmem& s, unsigned k, unsigned li,
                                            uint64_t pol) {
     const Chunk ch = s.list[li];
@@ -165,11 +163,13 @@ __device__ __forceinline__ void IssueChunk(const MegaParams& p, const MkSmem& s,
 
 // After every thread is done with chunk rg.n's stage (the barrier): the slot
 // takes chunk rg.n + kMkStages (unless the CTA is aborting), and the ring
-// moves on.
+// moves on.  The issuing thread's count of issued chunks (flags[5]) is read
+// by thread 0 only after a barrier.
 __device__ __forceinline__ void ReleaseChunk(const MegaParams& p, const MkSmem& s, Ring& rg) {
     ConsumerBar();
     const unsigned k = rg.n + kMkStages;
-    if (threadIdx.x == 0 && k < rg.total && s.flags[0] == 0) IssueChunk(p, s, k, rg.li, rg.pol);
+    // the last warp issues: warp 0 carries the per-chunk totals and digits
+    if (threadIdx.x == kMkThreads - 32 && k < rg.total && s.flags[0] == 0) IssueChunk(p, s, k, rg.li, rg.pol);
     ++rg.n;
     rg.li = rg.li + 1 == rg.len ? 0 : rg.li + 1;
 }
@@ -312,24 +312,6 @@ __device__ __forceinline__ void RmsNormDigits(const float* x, const float* w, in
     ConsumerBar();
 }
 
-// Digit planes and scales of the count blocks (start + i) mod nb of x (in
-// shared memory, block b at x + 32 b), stored at block b of dig / sx: eight
-// threads per block, four elements each (the block max by three shuffles).
-__device__ __forceinline__ void DigitsBlocks(const float* x, int start, int count, int nb, int8_t* dig,
-                                             int dstride, float* sx) {
-    const uint32_t xa = SmemAddr(x), da = SmemAddr(dig);
-    for (int k0 = 0; k0 < count * 8; k0 += 256) {  // count * 8 threads, groups of 8 share a trip
-        const int k = k0 + threadIdx.x;
-        const bool on = k < count * 8;
-        const int b = on ? (start + k / 8) % nb : 0, e = 4 * (k % 8);
-        float4 v = make_float4(0.f, 0.f, 0.f, 0.f);
-        if (on) v = LdsF32x4(xa + 4 * (b * 32 + e));
-        const float y[4] = {v.x, v.y, v.z, v.w};
-        const float sc = QuadDigits(y, on, da + b * 32 + e, dstride);
-        if (on && (k & 7) == 0) sx[b] = sc;
-    }
-    ConsumerBar();
-}
 
 // ---------------------------------------------------------------- MMA pieces
 struct LaneMma {
@@ -594,23 +576,6 @@ __host__ __device__ __forceinline__ int HeadSplit(const MegaParams& p, int G) {
     return p.n_heads * bph <= G ? bph : 1;
 }
 
-// FFN-B share of CTA c: the row-major chunk indices [q0, q1) of the R16 down
-// weight (ceil(dim/16) row tiles x hidden/32 blocks), equal to within one
-// chunk for every CTA, visited as pieces (row tile t, blocks b .. b+len-1)
-// of at most one row tile and one ring stage each.
-template <typename F>
-__device__ __forceinline__ void ForEachDownPiece(const MegaParams& p, int c, int G, F&& f) {
-    const int nj = p.hidden / 32;
-    const long long Q = static_cast<long long>((p.dim + 15) / 16) * nj;
-    const int q0 = static_cast<int>(Q * c / G), q1 = static_cast<int>(Q * (c + 1) / G);
-    const int smax = p.stage_bytes / kR16Chunk;
-    for (int q = q0; q < q1;) {
-        const int t = q / nj, b = q - t * nj;
-        const int len = min(min(q1 - q, nj - b), smax);
-        f(t, b, len);
-        q += len;
-    }
-}
 
 template <typename F>
 __device__ void ForEachChunk(const MegaParams& p, int c, int G, F&& f) {
@@ -621,7 +586,6 @@ __device__ void ForEachChunk(const MegaParams& p, int c, int G, F&& f) {
     const int ntiles_dim = (p.dim + 15) / 16;
     const uint32_t col_b = static_cast<uint32_t>(ntiles_dim) * kR16Chunk;
     const int nj = p.hidden / 32;
-    const int t_h = p.hidden / 16;
     const int t_lm = (p.vocab + 15) / 16;
     const int bph = p.hd / 32;  // wo block columns per head
     const int hsplit = HeadSplit(p, G);
@@ -635,13 +599,13 @@ __device__ void ForEachChunk(const MegaParams& p, int c, int G, F&& f) {
         for (int it = G - 1 - c; it < p.n_heads * hsplit; it += G)  // attention items (head, its wo columns)
             for (int j = (it % hsplit) * (bph / hsplit); j < (it % hsplit + 1) * (bph / hsplit); ++j)
                 f(Chunk{L.wo + size_t((it / hsplit) * bph + j) * col_b, nullptr, col_b, 0});
-        // FFN-A: gate row tile t and up row tile t in one stage
-        for (int t = c; t < t_h; t += G)
-            f(Chunk{L.gate + size_t(t) * tile_b, L.up + size_t(t) * tile_b, tile_b, tile_b});
-        // FFN-B: this CTA's share of the down rows, in pieces of one row tile
-        ForEachDownPiece(p, c, G, [&](int t, int b, int len) {
-            f(Chunk{L.down + (size_t(t) * nj + b) * kR16Chunk, nullptr, static_cast<uint32_t>(len) * kR16Chunk, 0});
-        });
+        // FFN: per 32-unit hidden block j, its gate rows, its up rows, its
+        // w_down block column (R16C)
+        for (int j = c; j < nj; j += G) {
+            f(Chunk{L.gate + size_t(2 * j) * tile_b, nullptr, 2 * tile_b, 0});
+            f(Chunk{L.up + size_t(2 * j) * tile_b, nullptr, 2 * tile_b, 0});
+            f(Chunk{L.down + size_t(j) * col_b, nullptr, col_b, 0});
+        }
     }
     // lm_head: two row tiles per stage
     for (int t2 = c; 2 * t2 < t_lm; t2 += G)
@@ -661,20 +625,13 @@ __device__ unsigned Consumers(const MegaParams& p, const MkSmem& s) {
     const int t_qkv = tq + 2 * tk;
     const int ntiles_dim = (p.dim + 15) / 16;
     const int nj = p.hidden / 32;
-    const int t_h = p.hidden / 16;
     const int t_lm = (p.vocab + 15) / 16;
     const int bph = p.hd / 32;
     // signals per step: one per QKV worker CTA, one per head, one per FFN
     // worker CTA; every CTA takes one LM ticket
-    // FFN-B shares: the CTAs with a non-empty range of the down chunks
-    const long long dQ = static_cast<long long>(ntiles_dim) * nj;
-    const int dq0 = static_cast<int>(dQ * c / G), dq1 = static_cast<int>(dQ * (c + 1) / G);
-    const bool has_down = dq1 > dq0;
-    const int nneed = min(dq1 - dq0, nj);
-    const int fdstride = DigitStride(nj);
     const int hsplit = HeadSplit(p, G);
-    const unsigned w_qkv = WorkerCount(G, t_qkv), w_att = p.n_heads * hsplit, w_ffa = WorkerCount(G, t_h),
-                   w_ffb = static_cast<unsigned>(min(static_cast<long long>(G), dQ)), w_lm = G;
+    const unsigned w_qkv = WorkerCount(G, t_qkv), w_att = p.n_heads * hsplit, w_ffn = WorkerCount(G, nj),
+                   w_lm = G;
     const int ctr_lm_ticket = kMkPhases * p.n_layers, ctr_token = kMkPhases * p.n_layers + 1;
     Ring rg;  // the chunk sequence thread 0 issued in the prologue, continued here
     rg.n = 0;
@@ -702,7 +659,7 @@ __device__ unsigned Consumers(const MegaParams& p, const MkSmem& s) {
                 }
                 if (l == 0) {
                     if (step > 0 && !WaitCounter(p, s, ctr_token, k1 - 1)) return rg.n;
-                } else if (!WaitCounter(p, s, kMkPhases * (l - 1) + 3, k1 * w_ffb)) {
+                } else if (!WaitCounter(p, s, kMkPhases * (l - 1) + 2, k1 * w_ffn)) {
                     return rg.n;
                 }
                 Trace(p, step, l, 0);
@@ -833,16 +790,18 @@ __device__ unsigned Consumers(const MegaParams& p, const MkSmem& s) {
                             }
                         } else {
                             int i0 = 0;
-                            if (base == 0) {  // the prefetched part of the row
+                            if (base == 0) {  // the prefetched part of the row, four chains
+                                float d4[4] = {0.f, 0.f, 0.f, 0.f};
 #pragma unroll
                                 for (int i = 0; i < 16; ++i)
                                     if (i < lpr) {
                                         const float4 qv = q4[i];
-                                        dot = fmaf(qv.x, kpre[i].x, dot);
-                                        dot = fmaf(qv.y, kpre[i].y, dot);
-                                        dot = fmaf(qv.z, kpre[i].z, dot);
-                                        dot = fmaf(qv.w, kpre[i].w, dot);
+                                        d4[i & 3] = fmaf(qv.x, kpre[i].x, d4[i & 3]);
+                                        d4[i & 3] = fmaf(qv.y, kpre[i].y, d4[i & 3]);
+                                        d4[i & 3] = fmaf(qv.z, kpre[i].z, d4[i & 3]);
+                                        d4[i & 3] = fmaf(qv.w, kpre[i].w, d4[i & 3]);
                                     }
+                                dot = (d4[0] + d4[1]) + (d4[2] + d4[3]);
                                 i0 = 16;
                             }
                             for (; i0 < lpr; i0 += 8) {  // 8 loads in flight
@@ -955,8 +914,9 @@ __device__ unsigned Consumers(const MegaParams& p, const MkSmem& s) {
                 Signal(p, kMkPhases * l + 1);
                 Trace(p, step, l, 3);
             }
-            // ---------------- FFN-A: gate and up row tiles, SwiGLU -> ff
-            if (c < t_h) {
+            // ---------------- FFN: per hidden block, gate and up rows, SwiGLU,
+            // then the block's w_down column into acc; one red.add pass
+            if (c < nj) {
                 LoadVecCg(s.nw, Lw.ffn_norm, p.dim);  // independent of the wait
                 if (!WaitCounter(p, s, kMkPhases * l + 1, k1 * w_att)) return rg.n;
                 Trace(p, step, l, 4);
@@ -965,64 +925,35 @@ __device__ unsigned Consumers(const MegaParams& p, const MkSmem& s) {
                 ConsumerBar();
                 RmsNormDigits(s.xs, s.nw, p.dim, p.eps, s.dig, dstride, s.sx, s.scratch);
                 Trace(p, step, l, 7);
-                for (int t = c; t < t_h; t += G) {
-                    float* red = RedBuf(s, rg);
-                    WaitChunk(p, s, rg);
-                    RowTilesDot(s, red, L, StagePtr(p, s, rg), 2, nb_dim, dstride);
-                    ReleaseChunk(p, s, rg);  // its barrier publishes red
-                    if (tid < 16) {
-                        const float g = RowTotal(red, 2, 0, tid), u = RowTotal(red, 2, 1, tid);
-                        const float sig = 1.0f / (1.0f + expf(-g));
-                        p.ff[t * 16 + tid] = g * sig * u;
+                for (int j = c; j < nj; j += G) {
+                    float gu[2];  // warp 0, lane r: gate and up of hidden unit 32 j + r
+#pragma unroll
+                    for (int part = 0; part < 2; ++part) {
+                        float* red = RedBuf(s, rg);
+                        WaitChunk(p, s, rg);
+                        RowTilesDot(s, red, L, StagePtr(p, s, rg), 2, nb_dim, dstride);
+                        ReleaseChunk(p, s, rg);  // its barrier publishes red
+                        if (tid < 32) gu[part] = RowTotal(red, 2, tid >> 4, tid & 15);
                     }
+                    if (tid < 32) {  // SwiGLU, then the block's digit planes
+                        const float sig = 1.0f / (1.0f + expf(-gu[0]));
+                        DigitsWarp(gu[0] * sig * gu[1], s.vdig, vstride, s.vsx);
+                    }
+                    ConsumerBar();
+                    WaitChunk(p, s, rg);
+                    ColumnDotSmem(L, StagePtr(p, s, rg), ntiles_dim, p.dim, s.vdig, vstride, s.vsx, s.acc);
+                    ReleaseChunk(p, s, rg);
                 }
+                // the residual x_mid joins through CTA 0
+                FlushRed(s.acc, xout, p.dim, c == 0 ? p.xmid : nullptr);
+                Trace(p, step, l, 6);
                 Signal(p, kMkPhases * l + 2);
                 Trace(p, step, l, 5);
-            }
-            // ---------------- FFN-B: this CTA's share of the down rows, + residual
-            if (has_down) {
-                if (!WaitCounter(p, s, kMkPhases * l + 2, k1 * w_ffa)) return rg.n;
-                Trace(p, step, l, 12);
-                // the ff blocks the share touches: (q0 + i) mod nj, i < nneed
-                for (int k = tid; k < nneed * 8; k += 256) {
-                    const int b = (dq0 + k / 8) % nj, e = 4 * (k % 8);
-                    CpAsync16(s.fx + b * 32 + e, p.ff + b * 32 + e);
-                }
-                CpAsyncWaitAll();
-                ConsumerBar();
-                DigitsBlocks(s.fx, dq0 % nj, nneed, nj, s.fdig, fdstride, s.fsx);
-                int t_first = -1, t_last = -1;
-                bool res_first = false;
-                ForEachDownPiece(p, c, G, [&](int t, int b, int len) {
-                    float* red = RedBuf(s, rg);
-                    WaitChunk(p, s, rg);
-                    RowTilesDotImpl<1>(s.fdig + b * 32, s.fsx + b, red, L, StagePtr(p, s, rg), len, fdstride);
-                    ReleaseChunk(p, s, rg);  // its barrier publishes red
-                    if (t_first < 0) {
-                        t_first = t;
-                        res_first = b == 0;
-                    }
-                    t_last = t;
-                    if (tid < 16) s.acc[t * 16 + tid] += RowTotal(red, 1, 0, tid);
-                });
-                Trace(p, step, l, 6);
-                // the CTA whose share starts a row tile at block 0 adds x_mid
-                for (int t = t_first; t <= t_last; ++t)
-                    if (tid < 16) {
-                        const int r = t * 16 + tid;
-                        if (r < p.dim) {
-                            const bool res = t > t_first || res_first;
-                            RedAdd(xout + r, s.acc[r] + (res ? __ldcg(p.xmid + r) : 0.0f));
-                        }
-                        s.acc[r] = 0.0f;
-                    }
-                Signal(p, kMkPhases * l + 3);
-                Trace(p, step, l, 13);
             }
         }
         // ---------------- lm_head + arg-max
         LoadVecCg(s.nw, p.final_norm, p.dim);  // independent of the wait
-        if (!WaitCounter(p, s, kMkPhases * (p.n_layers - 1) + 3, k1 * w_ffb)) return rg.n;
+        if (!WaitCounter(p, s, kMkPhases * (p.n_layers - 1) + 2, k1 * w_ffn)) return rg.n;
         Trace(p, step, p.n_layers, 0);
         float* xfin = p.xbuf[p.n_layers & 1];
         LoadVecCg(s.xs, xfin, p.dim);
@@ -1127,15 +1058,8 @@ __global__ void __launch_bounds__(kMkThreads, 1) MegaDecodeKernel(const MegaPara
     s.sx = reinterpret_cast<float*>(smem + kOffFixedEnd + 2 * vbytes + Round128(4 * size_t(DigitStride(nb_dim))));
     s.acc = reinterpret_cast<float*>(smem + kOffFixedEnd + 2 * vbytes + Round128(4 * size_t(DigitStride(nb_dim))) +
                                      Round128(4 * size_t(nb_dim)));
-    const int nj_all = p.hidden / 32;
-    size_t off2 = kOffFixedEnd + 3 * vbytes + Round128(4 * size_t(DigitStride(nb_dim))) + Round128(4 * size_t(nb_dim));
-    s.fx = reinterpret_cast<float*>(smem + off2);
-    off2 += Round128(4 * size_t(p.hidden));
-    s.fdig = reinterpret_cast<int8_t*>(smem + off2);
-    off2 += Round128(4 * size_t(DigitStride(nj_all)));
-    s.fsx = reinterpret_cast<float*>(smem + off2);
-    off2 += Round128(4 * size_t(nj_all));
-    const size_t list_off = off2;
+    const size_t list_off =
+        kOffFixedEnd + 3 * vbytes + Round128(4 * size_t(DigitStride(nb_dim))) + Round128(4 * size_t(nb_dim));
     for (int i = threadIdx.x; i < p.dim; i += kMkThreads) s.acc[i] = 0.0f;
     s.list = reinterpret_cast<Chunk*>(smem + list_off);
     s.ring = smem + list_off + Round128(sizeof(Chunk) * size_t(p.list_cap));
@@ -1179,21 +1103,15 @@ int MegaListCap(const MegaParams& p, int G) {
     auto per = [G](int items) { return (items + G - 1) / G; };  // items of one CTA at most
     const int t_qkv = (p.qd + 15) / 16 + 2 * ((p.kd + 15) / 16);
     const int t_lm = (p.vocab + 15) / 16;
-    const long long dQ = static_cast<long long>((p.dim + 15) / 16) * (p.hidden / 32);
-    const int share = static_cast<int>((dQ + G - 1) / G);  // down chunks of one CTA at most
-    const int smax = p.stage_bytes / kR16Chunk;
-    const int pieces = share / min(smax, p.hidden / 32) + 2;  // + the splits at row-tile ends
     const int hsplit = HeadSplit(p, G);
-    return p.n_layers * (per(t_qkv) + per(p.n_heads * hsplit) * (p.hd / 32 / hsplit) + per(p.hidden / 16) + pieces) +
+    return p.n_layers * (per(t_qkv) + per(p.n_heads * hsplit) * (p.hd / 32 / hsplit) + 3 * per(p.hidden / 32)) +
            per((t_lm + 1) / 2);
 }
 
 size_t MegaSmemBytes(const MegaParams& p) {
     const int nb_dim = p.dim / 32;
-    const int nj = p.hidden / 32;
     return kOffFixedEnd + 3 * Round128(4 * size_t(p.dim)) + Round128(4 * size_t(DigitStride(nb_dim))) +
-           Round128(4 * size_t(nb_dim)) + Round128(4 * size_t(p.hidden)) + Round128(4 * size_t(DigitStride(nj))) +
-           Round128(4 * size_t(nj)) + Round128(sizeof(Chunk) * size_t(p.list_cap)) +
+           Round128(4 * size_t(nb_dim)) + Round128(sizeof(Chunk) * size_t(p.list_cap)) +
            size_t(kMkStages) * p.stage_bytes;
 }
 

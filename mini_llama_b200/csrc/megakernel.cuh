@@ -8,10 +8,10 @@
 //   ATTO(l)  one query head: RoPE, KV write, attention over 0..pos, then the
 //            head's 64 outputs times its block columns of wo, accumulated into
 //            x_mid with red.add (x_mid starts as x)
-//   FFN-A(l) 16-row tiles of gate and up (the same rows of both), SwiGLU -> ff
-//   FFN-B(l) an equal share of the w_down chunks (row-tile major), its rows'
-//            partial sums accumulated into the next x with red.add (x starts
-//            at zero; the share that starts a row tile adds x_mid)
+//   FFN(l)   per 32-unit hidden block: its 32 gate and 32 up rows, SwiGLU,
+//            then its w_down block column; the CTA sums its columns in shared
+//            memory and adds them into the next x with one red.add pass (x
+//            starts at zero; CTA 0 adds x_mid)
 //   LM       16-row tiles of lm_head -> logits; per-CTA arg-max; the last CTA
 //            to finish picks the token and releases the next step
 // Phases (kMkPhases a layer) are ordered by global counters (release by an atomic add after a
@@ -22,8 +22,8 @@
 // released it.  (Without a separate copy warp each thread may hold up to 255
 // registers; with nine warps an SM sub-partition would cap it at 168.)
 //
-// All weights are in the R16 layout (row tiles, qmma.cuh); wo in its
-// column-major variant R16C so a head's block columns are contiguous.  Products are
+// All weights are in the R16 layout (row tiles, qmma.cuh); wo and w_down in
+// its column-major variant R16C so a block column is one contiguous copy.  Products are
 // the exact integer block sums of qmma.cuh (mma.m16n8k32.s8 on int8 digit
 // planes of the activations).
 //
@@ -41,7 +41,7 @@ namespace mlb {
 constexpr int kMkConsumerWarps = 8;
 constexpr int kMkThreads = kMkConsumerWarps * 32;
 constexpr int kMkStages = 4;
-constexpr int kMkPhases = 4;        // counters per layer: QKV, attention, FFN-A, FFN-B
+constexpr int kMkPhases = 3;        // counters per layer: QKV, attention, FFN
 constexpr int kMkAttnChunk = 256;   // positions per attention pass (one per consumer thread)
 constexpr int kMkTraceEvents = 16;  // timeline stamps per (step, layer, CTA)
 
@@ -53,7 +53,7 @@ struct MegaLayer {
     const uint8_t* wo;    // R16C [dim, qd]
     const uint8_t* gate;  // R16 [hidden, dim]
     const uint8_t* up;    // R16 [hidden, dim]
-    const uint8_t* down;  // R16 [dim, hidden]
+    const uint8_t* down;  // R16C [dim, hidden]
 };
 
 struct MegaParams {
@@ -72,7 +72,6 @@ struct MegaParams {
     float* xbuf[2];
     float* xmid;
     float* qkv;
-    float* ff;  // [hidden] SwiGLU output (FFN-A -> FFN-B)
     float* logits;
     float* am_val;
     int* am_idx;
@@ -88,9 +87,9 @@ struct MegaParams {
     // optional timeline: [step][layer 0..n_layers][event][CTA] %globaltimer
     // stamps; null when off.  Events: QKV 0 wait done, 11 input normalised,
     // 10 products stored, 1 signalled; attention 2 wait done, 8 softmax.V
-    // done, 9 O-projection flushed, 3 signalled; FFN-A 4 wait done, 7 input
-    // normalised, 5 signalled; FFN-B 12 wait done, 6 pieces done, 13
-    // signalled; layer n_layers (lm_head) 0 wait done, 1 ticket taken.
+    // done, 9 O-projection flushed, 3 signalled; FFN 4 wait done, 7 input
+    // normalised, 6 down-projection flushed, 5 signalled; layer n_layers
+    // (lm_head) 0 wait done, 1 ticket taken.
     unsigned long long* trace;
     size_t trace_cap;
 };

@@ -40,24 +40,21 @@ def summarise(t: np.ndarray) -> dict:
     """t: [steps, n_layers + 1, EVENTS, ctas] stamps (ns, 0 = not stamped)."""
     steps, lp1 = t.shape[0], t.shape[1]
     L = lp1 - 1
-    spans = {k: [] for k in ("qkv", "att", "ffn_gate_up", "ffn_down", "lm_head", "step")}
-    gaps = {k: [] for k in ("qkv_to_att", "att_to_gate_up", "gate_up_to_down", "down_to_next")}
+    spans = {k: [] for k in ("qkv", "att", "ffn", "lm_head", "step")}
+    gaps = {k: [] for k in ("qkv_to_att", "att_to_ffn", "ffn_to_next")}
     for st in range(1, steps):
         for l in range(L):
             e = t[st, l]
             q0, q1 = _first(e[0]), _last(e[1])
             a0, a1 = _first(e[2]), _last(e[3])
             f0, f1 = _first(e[4]), _last(e[5])
-            g0, g1 = _first(e[12]), _last(e[13])
             nxt = _first(t[st, l + 1, 0])
             spans["qkv"].append(q1 - q0)
             spans["att"].append(a1 - a0)
-            spans["ffn_gate_up"].append(f1 - f0)
-            spans["ffn_down"].append(g1 - g0)
+            spans["ffn"].append(f1 - f0)
             gaps["qkv_to_att"].append(a0 - q1)
-            gaps["att_to_gate_up"].append(f0 - a1)
-            gaps["gate_up_to_down"].append(g0 - f1)
-            gaps["down_to_next"].append(nxt - g1)
+            gaps["att_to_ffn"].append(f0 - a1)
+            gaps["ffn_to_next"].append(nxt - f1)
         spans["lm_head"].append(_last(t[st, L, 1]) - _first(t[st, L, 0]))
         if st + 1 < steps:
             spans["step"].append(_first(t[st + 1, 0, 0]) - _first(t[st, 0, 0]))
@@ -75,8 +72,7 @@ def summarise(t: np.ndarray) -> dict:
            "handover_us": {k: round(float(np.median(v)) / 1e3, 3) for k, v in gaps.items() if v},
            "per_cta_us": {"qkv_input": seg(0, 11), "qkv_products": seg(11, 10), "qkv_signal": seg(10, 1),
                           "att_softmax_v": seg(2, 8), "att_o_proj": seg(8, 9), "att_signal": seg(9, 3),
-                          "gate_up_input": seg(4, 7), "gate_up_rest": seg(7, 5),
-                          "down_products": seg(12, 6), "down_flush_signal": seg(6, 13)}}
+                          "ffn_input": seg(4, 7), "ffn_products": seg(7, 6), "ffn_signal": seg(6, 5)}}
     return out
 
 

@@ -76,7 +76,7 @@ def test_timeline_summary_of_synthetic_stamps():
     for st in range(steps):
         base = 100000 * (st + 1)
         for ev, us in ((0, 0), (11, 1), (10, 2), (1, 3), (2, 4), (8, 5), (9, 6), (3, 7),
-                       (4, 8), (7, 9), (5, 10), (12, 11), (6, 12), (13, 13)):
+                       (4, 8), (7, 9), (6, 10), (5, 13)):
             t[st, 0, ev, :] = base + 1000 * us
         t[st, 0, 1, 1] = base + 3500  # the second CTA signals QKV later
         t[st, 1, 0, :] = base + 14000
@@ -84,8 +84,9 @@ def test_timeline_summary_of_synthetic_stamps():
     out = timeline.summarise(t)
     assert out["span_us"]["qkv"] == 3.5
     assert out["handover_us"]["qkv_to_att"] == 0.5
-    assert out["span_us"]["ffn_down"] == 2.0
-    assert out["handover_us"]["down_to_next"] == 1.0  # last layer: to the lm_head wait
+    assert out["span_us"]["ffn"] == 5.0
+    assert out["handover_us"]["ffn_to_next"] == 1.0  # last layer: to the lm_head wait
+    assert out["per_cta_us"]["ffn_products"] == 1.0
     assert out["span_us"]["lm_head"] == 6.0
     assert out["span_us"]["step"] == 100.0
     assert out["per_cta_us"]["att_softmax_v"] == 1.0
