@@ -68,6 +68,7 @@ struct DeviceContext {
     size_t workspace_bytes = 0;
     void* pinned = nullptr;  // small pinned staging buffer for host<->device scalars
     size_t pinned_bytes = 0;
+    int* status = nullptr;   // device status word of the op kernels with bounded waits
 };
 
 DeviceContext& Ctx(int device);                     // creates on first use, makes device current

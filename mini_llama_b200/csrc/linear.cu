@@ -145,6 +145,10 @@ void QuantLinear(const char* caller, int device, int qtype, const float* x, cons
                 std::to_string(block_count));
     DeviceContext& c = Ctx(device);
     const uint8_t* wb = static_cast<const uint8_t*>(w);
+    if (rows >= kTcMinRows) {  // prefill-sized batches: tcgen05 tensor cores
+        LaunchTcLinear(c, qtype, x, wb, rows, in_features, out_features, bias, y, c.status);
+        return;
+    }
 
     for (int m0 = 0; m0 < rows;) {
         int M = std::min(rows - m0, kGemvMaxM);

@@ -538,6 +538,12 @@ struct GemvPlan {
 };
 
 // M = 1 launch of a decode-graph variant (pro/epi are GemvPrologue/GemvEpilogue).
+// Quantized linear for rows >= kTcMinRows on the tcgen05 tensor cores
+// (tc05.cu); status receives MLB_ERR_DEVICE_TIMEOUT if a bounded wait expires.
+constexpr int kTcMinRows = 64;
+void LaunchTcLinear(DeviceContext& c, int qtype, const float* x, const uint8_t* w, int M, int K, int N,
+                    const float* bias, float* y, int* status);
+
 void LaunchGemvDecode(int qtype, int pro, int epi, const GemvParams& p, const GemvPlan& plan,
                       cudaStream_t stream);
 

@@ -48,6 +48,8 @@ DeviceContext& Ctx(int device) {
         uint64_t keep = UINT64_MAX;  // never hand freed blocks back to the driver
         CheckCuda(cudaMemPoolSetAttribute(c->pool, cudaMemPoolAttrReleaseThreshold, &keep),
                   "cudaMemPoolSetAttribute");
+        CheckCuda(cudaMalloc(&c->status, 256), "cudaMalloc(status)");
+        CheckCuda(cudaMemset(c->status, 0, 256), "cudaMemset(status)");
         g_ctx[device] = c;
     }
     return *g_ctx[device];
@@ -191,6 +193,12 @@ int mlb_synchronize(int device) {
     return Guard([&] {
         DeviceContext& c = Ctx(device);
         CheckCuda(cudaStreamSynchronize(c.stream), "cudaStreamSynchronize");
+        int st = 0;
+        CheckCuda(cudaMemcpy(&st, c.status, sizeof(int), cudaMemcpyDeviceToHost), "cudaMemcpy(status)");
+        if (st != 0) {
+            CheckCuda(cudaMemset(c.status, 0, sizeof(int)), "cudaMemset(status)");
+            Fail(st, "a bounded device wait of an op kernel expired");
+        }
     });
 }
 

@@ -1,0 +1,66 @@
+"""Quantized linears for 64 rows and more (prefill batches), which run on the
+tcgen05 tensor cores (csrc/tc05.cu), against the oracle's fp32 linear
+(the reference CPU algorithm).  Tolerance as for every quantized linear:
+|a - e| <= 1e-4 * max(1, |e|)."""
+import numpy as np
+import pytest
+
+from oracle.binding import Q40, Q41, Q80, STREAM_W, STREAM_X
+from tests.test_gpu_kernels import LIN_TOL, QNAME, assert_close, bench_blocks, linear_gpu
+
+pytestmark = pytest.mark.gpu
+
+SMALL_SHAPES = [(896, 896), (4864, 896), (896, 4864)]
+
+
+@pytest.mark.parametrize("qtype", [Q80, Q40, Q41])
+@pytest.mark.parametrize("n,k", SMALL_SHAPES)
+@pytest.mark.parametrize("m", [64, 512])
+def test_prefill_linear_microbench_shapes(mlb, gpu, oracle, qtype, n, k, m):
+    blocks = bench_blocks(oracle, qtype, n, k)
+    x = oracle.normal(m * k, 2, STREAM_X + 2000 + n + k + m, 1.0).reshape(m, k)
+    expect = oracle.linear(qtype, x, blocks, n)
+    assert_close(linear_gpu(mlb, gpu, qtype, x, blocks, n), expect, LIN_TOL,
+                 f"{QNAME[qtype]} [{n},{k}] M={m}")
+
+
+@pytest.mark.parametrize("qtype", [Q80, Q40, Q41])
+def test_prefill_linear_lm_head(mlb, gpu, oracle, qtype):
+    n, k, m = 151936, 896, 64
+    blocks = bench_blocks(oracle, qtype, n, k)
+    x = oracle.normal(m * k, 2, STREAM_X + 3000, 1.0).reshape(m, k)
+    expect = oracle.linear(qtype, x, blocks, n)
+    assert_close(linear_gpu(mlb, gpu, qtype, x, blocks, n), expect, LIN_TOL,
+                 f"{QNAME[qtype]} lm_head M={m}")
+
+
+@pytest.mark.parametrize("qtype", [Q80, Q40, Q41])
+@pytest.mark.parametrize("m,k,n", [(64, 33, 7), (100, 129, 200), (130, 896, 131), (63, 64, 96)])
+def test_prefill_linear_ragged_with_bias(mlb, gpu, oracle, qtype, m, k, n):
+    """Partial row and column tiles, K not a multiple of 32 or 64, bias; 63
+    rows take the GEMV, 64 and more the tensor cores."""
+    w = oracle.normal(n * k, 2, STREAM_W + 4000 + n + k, 0.02).reshape(n, k)
+    blocks = oracle.quantize(qtype, w)
+    x = oracle.normal(m * k, 2, STREAM_X + 4000 + m + k, 1.0).reshape(m, k)
+    bias = oracle.normal(n, 2, 4999, 0.1)
+    expect = oracle.linear(qtype, x, blocks, n) + bias[None, :]
+    assert_close(linear_gpu(mlb, gpu, qtype, x, blocks, n, bias), expect, LIN_TOL,
+                 f"{QNAME[qtype]} M={m} K={k} N={n}")
+
+
+def test_prefill_linear_row_scales(mlb, gpu, oracle):
+    """Rows of very different magnitude (1e-6 .. 1e4) keep their relative
+    accuracy: each x row and W row has its own power-of-two scale."""
+    n, k, m = 256, 896, 128
+    w = oracle.normal(n * k, 2, STREAM_W + 5000, 0.02).reshape(n, k)
+    w[::7] *= 1e-3
+    blocks = oracle.quantize(Q80, w)
+    x = oracle.normal(m * k, 2, STREAM_X + 5000, 1.0).reshape(m, k)
+    x *= np.logspace(-6, 4, m, dtype=np.float64)[:, None].astype(np.float32)
+    x = x.astype(np.float32)
+    expect = oracle.linear(Q80, x, blocks, n)
+    got = linear_gpu(mlb, gpu, Q80, x, blocks, n)
+    # relative to each row's own scale
+    scale = np.maximum(np.abs(expect).max(axis=1, keepdims=True), 1e-30)
+    err = np.abs(got.astype(np.float64) - expect) / scale
+    assert float(err.max()) <= 1e-5, float(err.max())
