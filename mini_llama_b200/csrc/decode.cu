@@ -123,6 +123,9 @@ struct mlb_session {
     size_t mega_smem = 0;
     unsigned* counters = nullptr;
     size_t counter_bytes = 0;
+    unsigned long long* qkvt = nullptr;  // tagged q, k, v words (never match a stale tag)
+    size_t qkvt_bytes = 0;
+    unsigned tag_base = 1;               // next (step 0, layer 0) tag; 0 marks never written
     cudaGraph_t graph = nullptr;
     cudaGraphExec_t exec = nullptr;
     std::vector<void*> allocations;
@@ -479,6 +482,9 @@ void PrepareMega(mlb_session* s, DeviceContext& c) {
                               cudaMemcpyHostToDevice, c.stream),
               "cudaMemcpyAsync(layer table)");
     s->counter_bytes = size_t(kMkPhases * cf.n_layers + 2) * sizeof(unsigned);
+    s->qkvt_bytes = size_t(cf.n_heads + 2 * cf.n_kv_heads) * cf.head_dim * 8;
+    s->qkvt = static_cast<unsigned long long*>(DevAlloc(s, c, s->qkvt_bytes));
+    CheckCuda(cudaMemsetAsync(s->qkvt, 0, s->qkvt_bytes, c.stream), "cudaMemsetAsync(qkv words)");
     s->counters = static_cast<unsigned*>(DevAlloc(s, c, s->counter_bytes));
     float* x2 = static_cast<float*>(DevAlloc(s, c, size_t(cf.dim) * 4));
     MegaParams& p = s->mp;
@@ -507,7 +513,7 @@ void PrepareMega(mlb_session* s, DeviceContext& c) {
     p.xbuf[0] = s->x;
     p.xbuf[1] = x2;
     p.xmid = s->xmid;
-    p.qkv = s->qkv;
+    p.qkvt = s->qkvt;
     p.logits = s->logits;
     p.am_val = s->am_val;
     p.am_idx = s->am_idx;
@@ -527,7 +533,14 @@ void PrepareMega(mlb_session* s, DeviceContext& c) {
 // hist[pos + 1] receives the arg-max when pos + 1 >= gen_from.
 void RunMega(mlb_session* s, DeviceContext& c, int start_pos, int n_steps, int gen_from) {
     CheckCuda(cudaMemsetAsync(s->counters, 0, s->counter_bytes, c.stream), "cudaMemsetAsync(counters)");
+    const unsigned span = static_cast<unsigned>(n_steps) * static_cast<unsigned>(s->mp.n_layers);
+    if (s->tag_base > 0xF0000000u - span) {  // tags would wrap: start over on a cleared buffer
+        s->tag_base = 1;
+        CheckCuda(cudaMemsetAsync(s->qkvt, 0, s->qkvt_bytes, c.stream), "cudaMemsetAsync(qkv words)");
+    }
     MegaParams p = s->mp;
+    p.tag_base = s->tag_base;
+    s->tag_base += span;
     p.start_pos = start_pos;
     p.n_steps = n_steps;
     p.gen_from = gen_from;

@@ -25,6 +25,19 @@ __device__ __forceinline__ int LdRelaxedInt(const int* p) {
     return v;
 }
 
+// Tagged hand-over words: (tag << 32) | float bits, one single-copy-atomic
+// 64-bit store; a reader polls the word until its tag is the expected one.
+__device__ __forceinline__ void StTagged(unsigned long long* p, unsigned tag, float v) {
+    const unsigned long long w = (static_cast<unsigned long long>(tag) << 32) | __float_as_uint(v);
+    asm volatile("st.relaxed.gpu.global.u64 [%0], %1;" ::"l"(p), "l"(w) : "memory");
+}
+
+__device__ __forceinline__ unsigned long long LdTagged(const unsigned long long* p) {
+    unsigned long long w;
+    asm volatile("ld.relaxed.gpu.global.u64 %0, [%1];" : "=l"(w) : "l"(p) : "memory");
+    return w;
+}
+
 __device__ __forceinline__ void RedAdd(float* p, float v) {
     asm volatile("red.global.add.f32 [%0], %1;" ::"l"(p), "f"(v) : "memory");
 }
@@ -630,8 +643,7 @@ __device__ unsigned Consumers(const MegaParams& p, const MkSmem& s) {
     // signals per step: one per QKV worker CTA, one per head, one per FFN
     // worker CTA; every CTA takes one LM ticket
     const int hsplit = HeadSplit(p, G);
-    const unsigned w_qkv = WorkerCount(G, t_qkv), w_att = p.n_heads * hsplit, w_ffn = WorkerCount(G, nj),
-                   w_lm = G;
+    const unsigned w_att = p.n_heads * hsplit, w_ffn = WorkerCount(G, nj), w_lm = G;
     const int ctr_lm_ticket = kMkPhases * p.n_layers, ctr_token = kMkPhases * p.n_layers + 1;
     Ring rg;  // the chunk sequence thread 0 issued in the prologue, continued here
     rg.n = 0;
@@ -645,6 +657,7 @@ __device__ unsigned Consumers(const MegaParams& p, const MkSmem& s) {
         const unsigned k1 = static_cast<unsigned>(step + 1);
         for (int l = 0; l < p.n_layers; ++l) {
             const MegaLayer& Lw = p.layers[l];
+            const unsigned tag = p.tag_base + static_cast<unsigned>(step * p.n_layers + l);
             float* xin = p.xbuf[l & 1];
             float* xout = p.xbuf[(l + 1) & 1];
             // ---------------- QKV
@@ -677,11 +690,12 @@ __device__ unsigned Consumers(const MegaParams& p, const MkSmem& s) {
                 }
                 CpAsyncWaitAll();
                 ConsumerBar();
-                if (c == 0) {  // x_mid starts as x; the next x starts at zero
+                if (c == 0) {  // x_mid starts as x, the next x at zero; then the attention CTAs may add
                     for (int i = tid; i < p.dim; i += 256) {
                         p.xmid[i] = s.xs[i];
                         xout[i] = 0.0f;
                     }
+                    Signal(p, kMkPhases * l + 0);
                 }
                 RmsNormDigits(s.xs, s.nw, p.dim, p.eps, s.dig, dstride, s.sx, s.scratch);
                 Trace(p, step, l, 11);
@@ -699,12 +713,12 @@ __device__ unsigned Consumers(const MegaParams& p, const MkSmem& s) {
                         if (r < rows) {
                             float v = RowTotal(red, 1, 0, tid);
                             if (Lw.bias[seg]) v += i < 32 ? s.vec[16 * i + tid] : Lw.bias[seg][r];
-                            p.qkv[off + r] = v;
+                            StTagged(p.qkvt + off + r, tag, v);  // read by the attention CTAs directly
                         }
                     }
                 }
                 Trace(p, step, l, 10);
-                Signal(p, kMkPhases * l + 0);
+                ConsumerBar();
                 Trace(p, step, l, 1);
             }
             // ---------------- attention + O projection, one query head
@@ -737,18 +751,38 @@ __device__ unsigned Consumers(const MegaParams& p, const MkSmem& s) {
                 float* st = s.att + half;
                 LoadVecCg(ct, p.rope_cos + size_t(pos) * half, half);
                 LoadVecCg(st, p.rope_sin + size_t(pos) * half, half);
-                if (!WaitCounter(p, s, kMkPhases * l + 0, k1 * w_qkv)) return rg.n;
-                Trace(p, step, l, 2);
                 float* q = s.vec;
                 float* kn = s.vec + 128;
                 float* vn = s.vec + 256;
                 float* o = s.vec + 384;
-                LoadVecCg(q, p.qkv + h * hd, hd);
-                LoadVecCg(kn, p.qkv + p.qd + kvh * hd, hd);
-                LoadVecCg(vn, p.qkv + p.qd + p.kd + kvh * hd, hd);
+                // q of the head, k and v of its kv head: each thread polls
+                // its tagged words until this step's layer-l tag (bounded)
+                for (int i = tid; i < 3 * hd; i += 256) {
+                    const int part = i / hd, d = i - part * hd;
+                    const size_t src = part == 0 ? size_t(h) * hd + d
+                                                 : size_t(p.qd) + (part - 1) * p.kd + size_t(kvh) * hd + d;
+                    unsigned long long wv = 0;
+                    bool got = false;
+                    for (int it2 = 0; it2 < kMkSpin; ++it2) {
+                        wv = LdTagged(p.qkvt + src);
+                        if (static_cast<unsigned>(wv >> 32) == tag) {
+                            got = true;
+                            break;
+                        }
+                        if ((it2 & 255) == 255 && LdRelaxedInt(p.status) != 0) break;
+                    }
+                    if (!got) {
+                        atomicCAS(p.status, 0, MLB_ERR_DEVICE_TIMEOUT);
+                        s.flags[0] = 1;
+                    }
+                    (part == 0 ? q : (part == 1 ? kn : vn))[d] = __uint_as_float(static_cast<unsigned>(wv));
+                }
                 for (int i = tid; i < hd; i += 256) o[i] = 0.0f;
-                CpAsyncWaitAll();
                 ConsumerBar();
+                if (tid == 0) s.flags[4] = s.flags[0] == 0;
+                ConsumerBar();
+                if (!s.flags[4]) return rg.n;
+                Trace(p, step, l, 2);
                 // RoPE with the reference CPU tables (bit-exact with them)
                 for (int j = tid; j < half; j += 256) {
                     const int a = p.neox ? j : 2 * j, b2 = p.neox ? j + half : 2 * j + 1;
@@ -909,6 +943,7 @@ __device__ unsigned Consumers(const MegaParams& p, const MkSmem& s) {
                                   s.vdig + j * 32, vstride, s.vsx + j, s.acc);
                     ReleaseChunk(p, s, rg);
                 }
+                if (!WaitCounter(p, s, kMkPhases * l + 0, k1)) return rg.n;  // x_mid holds x
                 FlushRed(s.acc, p.xmid, p.dim, nullptr);
                 Trace(p, step, l, 9);
                 Signal(p, kMkPhases * l + 1);

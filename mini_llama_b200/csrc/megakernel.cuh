@@ -14,7 +14,9 @@
 //            starts at zero; CTA 0 adds x_mid)
 //   LM       16-row tiles of lm_head -> logits; per-CTA arg-max; the last CTA
 //            to finish picks the token and releases the next step
-// Phases (kMkPhases a layer) are ordered by global counters (release by an atomic add after a
+// QKV hands q, k, v to the attention CTAs as tagged 64-bit words (value and
+// the step's layer tag in one single-copy-atomic store) that the readers poll
+// directly; the other phases (kMkPhases a layer) are ordered by global counters (release by an atomic add after a
 // fence, acquire by polling).  Weights never depend on data, so each CTA
 // streams its whole schedule (bulk copies into a ring of mbarrier-guarded
 // stages) as far ahead as the ring allows, across phases and steps: thread 0
@@ -71,7 +73,8 @@ struct MegaParams {
     float* vc;
     float* xbuf[2];
     float* xmid;
-    float* qkv;
+    unsigned long long* qkvt;  // [qd + 2 kd] tagged q, k, v words (QKV -> attention)
+    unsigned tag_base;         // tag of (step 0, layer 0); (step, l) -> tag_base + step * n_layers + l
     float* logits;
     float* am_val;
     int* am_idx;
