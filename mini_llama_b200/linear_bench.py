@@ -8,7 +8,8 @@ device to each block type; x ~ N(0, 1); shapes [N, K] = [896, 896],
 through the public entry point (mlb_quant_linear: M <= 63 runs the GEMV, M >= 64
 the tcgen05 kernel, including its x pre-pass) with CUDA events on the
 library stream, after warm-up, with the L2 flushed (a 256 MB write) before
-every launch, and printed as one JSON line:
+every launch and all reps queued before the first is waited for (device time,
+not host launch latency), and printed as one JSON line:
   gbs     algorithmic bytes (W blocks + 4 M K + 4 M N) / time, against the
           measured HBM copy bandwidth (MEASURED_PEAKS.json) -- the bound for
           M <= 8
@@ -60,16 +61,20 @@ def time_case(lib, dev, torch, stream, qtype, n, k, m, reps=10):
 
     for _ in range(3):
         run()
-    total = 0.0
+    lib.call("mlb_synchronize", dev)
+    # every rep is queued behind its own L2 flush (a 256 MB write that keeps
+    # the GPU busy while the host queues the rep), so the events bracket
+    # device time only, not host launch latency
+    events = []
     for _ in range(reps):
         lib.call("mlb_memset", dev, flush, 1, 256 << 20)
         e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
         e0.record(stream)
         run()
         e1.record(stream)
-        e1.synchronize()
-        total += e0.elapsed_time(e1) / 1e3
+        events.append((e0, e1))
     lib.call("mlb_synchronize", dev)
+    total = sum(e0.elapsed_time(e1) for e0, e1 in events) / 1e3
     for p in (w, xs, flush):
         lib.free(dev, p)
     secs = total / reps

@@ -64,3 +64,41 @@ def test_prefill_linear_row_scales(mlb, gpu, oracle):
     scale = np.maximum(np.abs(expect).max(axis=1, keepdims=True), 1e-30)
     err = np.abs(got.astype(np.float64) - expect) / scale
     assert float(err.max()) <= 1e-5, float(err.max())
+
+
+@pytest.mark.parametrize("qtype", [Q80, Q40, Q41])
+def test_prefill_linear_large_blocks_rescaled(mlb, gpu, oracle, qtype):
+    """Weights around 1e4: block scales whose |w| bound reaches 2^15 would
+    overflow fp16 unscaled, so those tiles are recomputed with per-row
+    power-of-two scales.  Tolerance 2e-6 of sum_k |x_k w_nk| per output."""
+    n, k, m = 300, 896, 96
+    w = oracle.normal(n * k, 2, STREAM_W + 6000, 1e4).reshape(n, k)
+    blocks = oracle.quantize(qtype, w)
+    x = oracle.normal(m * k, 2, STREAM_X + 6000, 1.0).reshape(m, k)
+    expect = oracle.linear(qtype, x, blocks, n)
+    got = linear_gpu(mlb, gpu, qtype, x, blocks, n).astype(np.float64)
+    # error against each output's own scale sum_k |x_k w_nk| (outputs near
+    # zero come from cancellation between terms of ~1e4, where any two fp32
+    # summation orders differ by ~1e-7 of that sum)
+    wd = oracle.dequantize(qtype, blocks, n, k).astype(np.float64)
+    scale = np.abs(x.astype(np.float64)) @ np.abs(wd).T
+    err = float((np.abs(got - expect) / scale).max())
+    assert err <= 2e-6, f"{QNAME[qtype]} |w|~1e4: {err:.3e}"
+
+
+@pytest.mark.parametrize("qtype", [Q80, Q40, Q41])
+def test_prefill_linear_subnormal_halves(mlb, gpu, oracle, qtype):
+    """Weights around 1e-4: fp16 block scales and many hi / lo halves are
+    subnormal; the products stay exact (relative error against the largest
+    output, which is ~1e-3, so the absolute floor of the usual tolerance
+    cannot hide a loss)."""
+    n, k, m = 256, 896, 64
+    w = oracle.normal(n * k, 2, STREAM_W + 7000, 1e-4).reshape(n, k)
+    blocks = oracle.quantize(qtype, w)
+    x = oracle.normal(m * k, 2, STREAM_X + 7000, 1.0).reshape(m, k)
+    expect = oracle.linear(qtype, x, blocks, n)
+    got = linear_gpu(mlb, gpu, qtype, x, blocks, n).astype(np.float64)
+    scale = float(np.abs(expect).max())
+    assert scale > 0
+    err = float(np.abs(got - expect).max()) / scale
+    assert err <= 1e-5, err
