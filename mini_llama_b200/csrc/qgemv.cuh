@@ -537,13 +537,16 @@ struct GemvPlan {
     size_t smem = 0;
 };
 
-// M = 1 launch of a decode-graph variant (pro/epi are GemvPrologue/GemvEpilogue).
 // Quantized linear for rows >= kTcMinRows on the tcgen05 tensor cores
 // (tc05.cu); status receives MLB_ERR_DEVICE_TIMEOUT if a bounded wait expires.
-constexpr int kTcMinRows = 64;
+// Up to kGemvMaxM rows one GEMV pass is faster; beyond, the GEMV would stream
+// the weights once per kGemvMaxM rows while the tensor-core kernel's time
+// hardly depends on the row count below 64.
+constexpr int kTcMinRows = kGemvMaxM + 1;
 void LaunchTcLinear(DeviceContext& c, int qtype, const float* x, const uint8_t* w, int M, int K, int N,
                     const float* bias, float* y, int* status);
 
+// M = 1 launch of a decode-graph variant (pro/epi are GemvPrologue/GemvEpilogue).
 void LaunchGemvDecode(int qtype, int pro, int epi, const GemvParams& p, const GemvPlan& plan,
                       cudaStream_t stream);
 

@@ -1,4 +1,4 @@
-// Quantized linear for M >= 64 rows (prefill): y = x W^T (+ bias) on the
+// Quantized linear for M >= 9 rows (prefill): y = x W^T (+ bias) on the
 // 5th-generation tensor cores (tcgen05.mma, accumulator in tensor memory).
 // Replaces the reference's Q8_0 / Q4_0 / Q4_1 linear kernels
 // (src/cuda_quant.cu:40-135) for batches of rows.
@@ -38,10 +38,12 @@
 //              two rows from the ring into the stage's hi / lo images, and
 //              each warp arrives on wfull.  Afterwards they are the epilogue.
 //   warp 8     bulk-copies the x hi / lo images of each stage (written by the
-//              pre-pass TcPrepX), completing on xfull.
+//              pre-pass TcPrepX) into their own ring of 64 KB (4 stages at
+//              MX = 256, up to 16 for small MX), completing on xfull.
 //   warp 9     allocates tensor memory; one lane issues the 3 NW MMAs of a
 //              stage (3 products x NW sub-tiles) and commits them to the
-//              stage's empty barrier, and after the last stage to accfull.
+//              stage's W and x empty barriers, and after the last stage to
+//              accfull.
 // The pre-pass, this kernel and the split-K sum are chained with programmatic
 // dependent launch: each starts its independent prologue while the previous
 // one runs and waits (griddepcontrol.wait) before touching its output.
@@ -60,11 +62,12 @@ namespace {
 constexpr int kTcRows = 128;                        // W rows per MMA (M of the instruction)
 constexpr int kTcMaxX = 256;                        // x rows per MMA at most (N of the instruction)
 constexpr int kTcK = 16;                            // elements of K per stage: half a block
-constexpr int kTcStages = 4;
+constexpr int kTcStages = 4;                        // W image stages in flight
 constexpr int kTcWImg = kTcRows * kTcK * 2;         // one fp16 image of a 128-row W sub-tile
 constexpr int kTcWBytes = 2 * kTcWImg;              // its hi + lo images
-constexpr int kTcXOff = 2 * kTcWBytes;              // x images follow room for two W sub-tiles
-constexpr int kTcStageBytes = kTcXOff + 2 * kTcMaxX * kTcK * 2;  // 32 KB
+constexpr int kTcStageBytes = 2 * kTcWBytes;        // room for two W sub-tiles: 16 KB
+constexpr int kTcXRing = 64 * 1024;                 // x image stages: 64 MX bytes each
+constexpr int kTcXSlotsMax = 16;
 constexpr int kTcRawSlots = 3;                      // raw windows in flight
 constexpr int kTcHeader = 2048;
 constexpr int kTcDqWarps = 8;
@@ -217,7 +220,8 @@ struct TcBlock {
 
 template <int QT>
 constexpr size_t TcSmemBytes() {
-    return kTcHeader + size_t(kTcStages) * kTcStageBytes + size_t(kTcRawSlots) * 2 * kTcRows * TcBlock<QT>::kRawRow;
+    return kTcHeader + size_t(kTcStages) * kTcStageBytes + kTcXRing +
+           size_t(kTcRawSlots) * 2 * kTcRows * TcBlock<QT>::kRawRow;
 }
 
 // The raw bytes one lane converts: the block's fp16 d (and Q4_1's m in the
@@ -328,9 +332,10 @@ __device__ __forceinline__ void TcConvert(const TcRaw& r, int h, float mul, uint
 }
 
 struct TcShared {
-    uint64_t xfull[kTcStages];
+    uint64_t xfull[kTcXSlotsMax];
+    uint64_t xempty[kTcXSlotsMax];
     uint64_t wfull[kTcStages];
-    uint64_t empty[kTcStages];
+    uint64_t wempty[kTcStages];
     uint64_t rawfull[kTcRawSlots];
     uint64_t rawempty[kTcRawSlots];
     uint64_t accfull;
@@ -363,7 +368,8 @@ __global__ void __launch_bounds__(kTcThreads, 1) TcLinearKernel(const TcArgs a) 
     extern __shared__ __align__(1024) uint8_t smem[];
     TcShared& sh = *reinterpret_cast<TcShared*>(smem);
     uint8_t* stages = smem + kTcHeader;
-    uint8_t* raw = stages + kTcStages * kTcStageBytes;
+    uint8_t* xring = stages + kTcStages * kTcStageBytes;
+    uint8_t* raw = xring + kTcXRing;
     constexpr int kItems = NW;                              // W rows per dequant thread
     constexpr int kBB = TcBlock<QT>::kBytes;
     constexpr int kRawRow = TcBlock<QT>::kRawRow;
@@ -373,15 +379,19 @@ __global__ void __launch_bounds__(kTcThreads, 1) TcLinearKernel(const TcArgs a) 
     const int n0 = blockIdx.y * NW * kTcRows, m0 = mt * a.mx;
     const int kb0 = split * a.kper, kb1 = min(a.nb, kb0 + a.kper), nk = kb1 - kb0, nst = 2 * nk;
     const int mx = a.mx;
+    const int xslots = min(kTcXSlotsMax, kTcXRing / (64 * mx));  // x image stages in flight
     const size_t rowbytes = size_t(a.nb) * kBB;
     const uintptr_t wend = reinterpret_cast<uintptr_t>(a.w) + size_t(a.N) * rowbytes;
     const volatile int* abort = &sh.abort;
 
     if (tid == 0) {
         for (int i = 0; i < kTcStages; ++i) {
-            MbarInit(&sh.xfull[i], 1);
             MbarInit(&sh.wfull[i], kTcDqWarps);
-            MbarInit(&sh.empty[i], 1);
+            MbarInit(&sh.wempty[i], 1);
+        }
+        for (int i = 0; i < kTcXSlotsMax; ++i) {
+            MbarInit(&sh.xfull[i], 1);
+            MbarInit(&sh.xempty[i], 1);
         }
         for (int i = 0; i < kTcRawSlots; ++i) {
             MbarInit(&sh.rawfull[i], kTcDqWarps);  // + the bytes of the warps' bulk copies
@@ -483,7 +493,7 @@ __global__ void __launch_bounds__(kTcThreads, 1) TcLinearKernel(const TcArgs a) 
 #pragma unroll
                     for (int h = 0; h < 2; ++h) {
                         const int git = pass * nst + 2 * b + h, slot = git % kTcStages, use = git / kTcStages;
-                        if (use > 0 && !MbarWaitFor(&sh.empty[slot], (use - 1) & 1, kTcWaitNs, abort)) {
+                        if (use > 0 && !MbarWaitFor(&sh.wempty[slot], (use - 1) & 1, kTcWaitNs, abort)) {
                             ok = false;
                             break;
                         }
@@ -528,21 +538,21 @@ __global__ void __launch_bounds__(kTcThreads, 1) TcLinearKernel(const TcArgs a) 
                 const uint32_t bytes = static_cast<uint32_t>(mx) * kTcK * 4;
                 int issued = 0;
                 for (int it = 0; it < nst; ++it) {
-                    const int git = pass * nst + it, slot = git % kTcStages, use = git / kTcStages;
-                    if (use > 0 && !MbarWaitFor(&sh.empty[slot], (use - 1) & 1, kTcWaitNs, abort)) {
+                    const int git = pass * nst + it, slot = git % xslots, use = git / xslots;
+                    if (use > 0 && !MbarWaitFor(&sh.xempty[slot], (use - 1) & 1, kTcWaitNs, abort)) {
                         if (!*abort) TcFail(sh, a.status);
                         break;
                     }
                     if (*abort) break;
                     MbarExpectTx(&sh.xfull[slot], bytes);
-                    BulkLoad(stages + size_t(slot) * kTcStageBytes + kTcXOff,
-                             a.ximg + (size_t(mt) * a.kst + 2 * kb0 + it) * bytes, bytes, &sh.xfull[slot]);
+                    BulkLoad(xring + size_t(slot) * bytes, a.ximg + (size_t(mt) * a.kst + 2 * kb0 + it) * bytes, bytes,
+                             &sh.xfull[slot]);
                     issued = it + 1;
                 }
                 // copies still in flight land before the CTA moves on
-                for (int it = max(0, issued - kTcStages); it < issued; ++it) {
+                for (int it = max(0, issued - xslots); it < issued; ++it) {
                     const int git = pass * nst + it;
-                    if (!MbarWaitFor(&sh.xfull[git % kTcStages], (git / kTcStages) & 1, kTcWaitNs, nullptr))
+                    if (!MbarWaitFor(&sh.xfull[git % xslots], (git / xslots) & 1, kTcWaitNs, nullptr))
                         TcFail(sh, a.status);
                 }
             }
@@ -554,14 +564,15 @@ __global__ void __launch_bounds__(kTcThreads, 1) TcLinearKernel(const TcArgs a) 
                 int last = -1;  // stage (of this pass) of the last commit
                 for (int it = 0; it < nst; ++it) {
                     const int git = pass * nst + it, slot = git % kTcStages, use = git / kTcStages;
-                    if (!MbarWaitFor(&sh.xfull[slot], use & 1, kTcWaitNs, abort) ||
+                    const int xs = git % xslots, xuse = git / xslots;
+                    if (!MbarWaitFor(&sh.xfull[xs], xuse & 1, kTcWaitNs, abort) ||
                         !MbarWaitFor(&sh.wfull[slot], use & 1, kTcWaitNs, abort)) {
                         if (!*abort) TcFail(sh, a.status);
                         break;
                     }
                     TcFenceAfter();
                     const uint32_t sbase = SmemAddr(stages + size_t(slot) * kTcStageBytes);
-                    const uint32_t xb = sbase + kTcXOff;
+                    const uint32_t xb = SmemAddr(xring) + xs * (64 * mx);
                     const uint64_t bhi = SmemDesc(xb, xlbo), blo = SmemDesc(xb + mx * kTcK * 2, xlbo);
 #pragma unroll
                     for (int t = 0; t < NW; ++t) {
@@ -572,7 +583,8 @@ __global__ void __launch_bounds__(kTcThreads, 1) TcLinearKernel(const TcArgs a) 
                         TcMma(d, alo, bhi, idesc, 1);
                         TcMma(d, ahi, blo, idesc, 1);
                     }
-                    TcCommit(&sh.empty[slot]);
+                    TcCommit(&sh.wempty[slot]);
+                    TcCommit(&sh.xempty[xs]);
                     last = it;
                 }
                 if (last == nst - 1 && nst > 0) {
@@ -580,7 +592,7 @@ __global__ void __launch_bounds__(kTcThreads, 1) TcLinearKernel(const TcArgs a) 
                 } else if (last >= 0) {
                     // aborted: the MMAs issued so far finish before tensor memory is freed
                     const int git = pass * nst + last;
-                    if (!MbarWaitFor(&sh.empty[git % kTcStages], (git / kTcStages) & 1, kTcWaitNs, nullptr))
+                    if (!MbarWaitFor(&sh.wempty[git % kTcStages], (git / kTcStages) & 1, kTcWaitNs, nullptr))
                         TcFail(sh, a.status);
                 }
             }

@@ -5,7 +5,7 @@
 Weights W ~ N(0, 0.02) (seeded generator on the device) quantized on the
 device to each block type; x ~ N(0, 1); shapes [N, K] = [896, 896],
 [4864, 896], [896, 4864], [151936, 896]; M rows of x.  Each case is timed
-through the public entry point (mlb_quant_linear: M <= 63 runs the GEMV, M >= 64
+through the public entry point (mlb_quant_linear: M <= 8 runs the GEMV, M >= 9
 the tcgen05 kernel, including its x pre-pass) with CUDA events on the
 library stream, after warm-up, with the L2 flushed (a 256 MB write) before
 every launch and all reps queued before the first is waited for (device time,
@@ -106,7 +106,7 @@ def main(argv=None) -> int:
                                   "gbs": round(gbs, 1), "hbm_frac": round(gbs / pk["hbm_gbs"], 3),
                                   "tflops": round(tflops, 2),
                                   "bf16_frac": round(tflops / pk["bf16_tflops"], 4),
-                                  "path": "tcgen05" if m >= 64 else "gemv", "peaks": pk["source"]}),
+                                  "path": "tcgen05" if m >= 9 else "gemv", "peaks": pk["source"]}),
                       flush=True)
     return 0
 

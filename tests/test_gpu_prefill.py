@@ -1,4 +1,4 @@
-"""Quantized linears for 64 rows and more (prefill batches), which run on the
+"""Quantized linears for 9 rows and more (prefill batches), which run on the
 tcgen05 tensor cores (csrc/tc05.cu), against the oracle's fp32 linear
 (the reference CPU algorithm).  Tolerance as for every quantized linear:
 |a - e| <= 1e-4 * max(1, |e|)."""
@@ -15,7 +15,7 @@ SMALL_SHAPES = [(896, 896), (4864, 896), (896, 4864)]
 
 @pytest.mark.parametrize("qtype", [Q80, Q40, Q41])
 @pytest.mark.parametrize("n,k", SMALL_SHAPES)
-@pytest.mark.parametrize("m", [64, 512])
+@pytest.mark.parametrize("m", [16, 64, 512])
 def test_prefill_linear_microbench_shapes(mlb, gpu, oracle, qtype, n, k, m):
     blocks = bench_blocks(oracle, qtype, n, k)
     x = oracle.normal(m * k, 2, STREAM_X + 2000 + n + k + m, 1.0).reshape(m, k)
@@ -35,10 +35,11 @@ def test_prefill_linear_lm_head(mlb, gpu, oracle, qtype):
 
 
 @pytest.mark.parametrize("qtype", [Q80, Q40, Q41])
-@pytest.mark.parametrize("m,k,n", [(64, 33, 7), (100, 129, 200), (130, 896, 131), (63, 64, 96)])
+@pytest.mark.parametrize("m,k,n", [(64, 33, 7), (100, 129, 200), (130, 896, 131), (63, 64, 96), (9, 896, 300),
+                                   (8, 64, 96), (37, 4864, 129)])
 def test_prefill_linear_ragged_with_bias(mlb, gpu, oracle, qtype, m, k, n):
-    """Partial row and column tiles, K not a multiple of 32 or 64, bias; 63
-    rows take the GEMV, 64 and more the tensor cores."""
+    """Partial row and column tiles, K not a multiple of 32 or 64, bias; 8
+    rows take the GEMV, 9 and more the tensor cores."""
     w = oracle.normal(n * k, 2, STREAM_W + 4000 + n + k, 0.02).reshape(n, k)
     blocks = oracle.quantize(qtype, w)
     x = oracle.normal(m * k, 2, STREAM_X + 4000 + m + k, 1.0).reshape(m, k)
