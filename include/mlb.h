@@ -307,6 +307,47 @@ int mlb_session_trace(mlb_session* session, unsigned long long* device_buffer, s
 /* Device pointers of the session KV cache. */
 int mlb_session_kv_cache(mlb_session* session, float** key_cache, float** value_cache);
 
+/* ------------------------------------------------------------ batched decode
+ * A batch of independent sequences decoded in lockstep through one model:
+ * every step feeds one token per sequence (prompt tokens first, then the
+ * greedy choice), so each linear runs on `batch` rows (the GEMV up to 8 rows,
+ * the tcgen05 tensor cores from 9) and attention runs batched.  No reference
+ * counterpart: the reference decodes one sequence at a time (ForwardBatch,
+ * src/forward.cpp:668-684, loops ForwardToken); per sequence the computation
+ * is that of mlb_session_generate, so the greedy tokens match it.
+ *
+ * Tensor parallelism: tp_size processes, one GPU each, build the same model
+ * and each create a batch with its tp_rank and the same NCCL id (from
+ * mlb_nccl_unique_id on one rank, shared by the caller).  Every linear's
+ * output rows are split into tp_size contiguous slices -- q/k/v by KV-head
+ * group, so each rank attends with its own KV heads and holds only their
+ * cache -- and the slices are all-gathered with NCCL before the next step that
+ * needs whole rows; the lm_head is split by vocabulary and the per-rank
+ * arg-maxes are merged (first maximum wins).  tp_size must divide n_kv_heads,
+ * dim, hidden_dim and vocab_size.  One step (all layers and the collectives)
+ * is captured once as a CUDA graph. */
+typedef struct mlb_batch mlb_batch;
+#define MLB_NCCL_ID_BYTES 128
+/* An NCCL unique id (MLB_NCCL_ID_BYTES bytes) for one tensor-parallel group. */
+int mlb_nccl_unique_id(void* id);
+/* The slices rank tp_rank owns, as 5 half-open ranges (10 ints): query heads,
+ * KV heads, dim rows (wo, w_down), hidden rows (w_gate, w_up), vocabulary
+ * rows (lm_head).  MLB_ERR_UNSUPPORTED when tp_size does not divide them. */
+int mlb_batch_shard(const mlb_model_config* config, int tp_rank, int tp_size, int* ranges);
+/* nccl_id may be NULL when tp_size == 1. */
+int mlb_batch_create(mlb_model* model, int batch, int tp_rank, int tp_size, const void* nccl_id,
+                     mlb_batch** out);
+int mlb_batch_destroy(mlb_batch* batch);
+/* Greedy continuation of `batch` prompts of n_prompt tokens each (host
+ * [batch][n_prompt]) by n_new tokens (host out_tokens [batch][n_new]), from
+ * position 0.  prefill_ms / decode_ms (may be NULL) receive the device time of
+ * the n_prompt prompt steps and of the n_new - 1 further steps. */
+int mlb_batch_generate(mlb_batch* batch, const int* prompts, int n_prompt, int n_new, int* out_tokens,
+                       float* prefill_ms, float* decode_ms);
+/* Device pointer of the last step's logits slice ([batch][cols], this rank's
+ * vocabulary rows col0 .. col0 + cols - 1). */
+int mlb_batch_logits(mlb_batch* batch, const float** logits, int* cols, int* col0);
+
 #ifdef __cplusplus
 }
 #endif

@@ -103,7 +103,16 @@ SIGNATURES = {
     "mlb_session_use_persistent": (_i, [_vp, _i]),
     "mlb_session_trace": (_i, [_vp, _vp, _sz]),
     "mlb_session_kv_cache": (_i, [_vp, _pp, _pp]),
+    "mlb_nccl_unique_id": (_i, [_vp]),
+    "mlb_batch_shard": (_i, [ctypes.POINTER(ModelConfig), _i, _i, _pi]),
+    "mlb_batch_create": (_i, [_vp, _i, _i, _i, _vp, _pp]),
+    "mlb_batch_destroy": (_i, [_vp]),
+    "mlb_batch_generate": (_i, [_vp, _vp, _i, _i, _vp, ctypes.POINTER(ctypes.c_float),
+                                ctypes.POINTER(ctypes.c_float)]),
+    "mlb_batch_logits": (_i, [_vp, _pp, _pi, _pi]),
 }
+
+NCCL_ID_BYTES = 128
 
 
 class MlbError(RuntimeError):

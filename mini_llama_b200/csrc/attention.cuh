@@ -54,6 +54,8 @@ struct AttnParams {
     // decode-graph mode: q/k/v raw from the QKV GEMV, RoPE here, KV write here
     int fused_rope;
     const float* kv_new;    // k at kv_new[kvh*hd], v at kv_new[n_kv*hd + kvh*hd]
+    const float* v_new;     // when set, v at v_new[kvh*hd] instead
+    size_t kv_batch_stride; // floats between sequences' kv_new (and v_new) rows
     const float* rope_cos;  // [max_seq_len][hd/2]
     const float* rope_sin;
     int neox;
@@ -128,8 +130,10 @@ __global__ void __launch_bounds__(kAttnThreads) AttnSplitKernel(const AttnParams
             qs[g * hd + c2] = __fadd_rn(__fmul_rn(x0, sn), __fmul_rn(x1, cs));
         }
         if (own_new) {
-            const float* kn = p.kv_new + size_t(kvh) * hd;
-            const float* vn = p.kv_new + size_t(p.n_kv) * hd + size_t(kvh) * hd;
+            const float* kn = p.kv_new + size_t(b) * p.kv_batch_stride + size_t(kvh) * hd;
+            const float* vn = (p.v_new ? p.v_new + size_t(b) * p.kv_batch_stride
+                                       : p.kv_new + size_t(b) * p.kv_batch_stride + size_t(p.n_kv) * hd) +
+                              size_t(kvh) * hd;
             float* kd = kbase + size_t(pos) * pos_stride;
             float* vd = vbase + size_t(pos) * pos_stride;
             const int r = pos - p0;

@@ -128,7 +128,7 @@ void LaunchFallback(const float* x, const uint8_t* w, const float* bias, float* 
 }
 
 // Shared by the entry points: validation with the reference's messages
-// (src/cuda_quant.cu:184-210), then one launch per chunk of <= 8 rows.
+// (src/cuda_quant.cu:184-210), then LinearRows.
 void QuantLinear(const char* caller, int device, int qtype, const float* x, const void* w,
                  size_t block_count, int rows, int in_features, int out_features,
                  const float* bias, float* y) {
@@ -144,9 +144,13 @@ void QuantLinear(const char* caller, int device, int qtype, const float* x, cons
             "block count mismatch: expected " + std::to_string(expected) + ", got " +
                 std::to_string(block_count));
     DeviceContext& c = Ctx(device);
-    const uint8_t* wb = static_cast<const uint8_t*>(w);
+    LinearRows(c, qtype, x, static_cast<const uint8_t*>(w), rows, in_features, out_features, bias, y);
+}
+
+void LinearRows(DeviceContext& c, int qtype, const float* x, const uint8_t* wb, int rows, int in_features,
+                int out_features, const float* bias, float* y, void* tc_workspace) {
     if (rows >= kTcMinRows) {  // prefill-sized batches: tcgen05 tensor cores
-        LaunchTcLinear(c, qtype, x, wb, rows, in_features, out_features, bias, y, c.status);
+        LaunchTcLinear(c, qtype, x, wb, rows, in_features, out_features, bias, y, c.status, tc_workspace);
         return;
     }
 

@@ -542,9 +542,19 @@ struct GemvPlan {
 // Up to kGemvMaxM rows one GEMV pass is faster; beyond, the GEMV would stream
 // the weights once per kGemvMaxM rows while the tensor-core kernel's time
 // hardly depends on the row count below 64.
+// workspace: TcWorkspaceBytes(M, K, N, sm_count) bytes of device memory (a
+// caller that captures the launch into a CUDA graph owns it), or null for the
+// context's grow-only workspace.
 constexpr int kTcMinRows = kGemvMaxM + 1;
 void LaunchTcLinear(DeviceContext& c, int qtype, const float* x, const uint8_t* w, int M, int K, int N,
-                    const float* bias, float* y, int* status);
+                    const float* bias, float* y, int* status, void* workspace = nullptr);
+size_t TcWorkspaceBytes(int M, int K, int N, int sm_count);
+
+// Quantized linear over GGUF blocks for any row count (the GEMV up to
+// kGemvMaxM rows at a time below kTcMinRows, the tensor cores above), on the
+// context's stream; tc_workspace as for LaunchTcLinear.
+void LinearRows(DeviceContext& c, int qtype, const float* x, const uint8_t* w, int rows, int K, int N,
+                const float* bias, float* y, void* tc_workspace = nullptr);
 
 // M = 1 launch of a decode-graph variant (pro/epi are GemvPrologue/GemvEpilogue).
 void LaunchGemvDecode(int qtype, int pro, int epi, const GemvParams& p, const GemvPlan& plan,

@@ -705,17 +705,33 @@ void LaunchTcKernel(DeviceContext& c, dim3 grid, const TcArgs& a) {
     Launch("TcLinearKernel", TcLinearKernel<QT, NW>, grid, dim3(kTcThreads), smem, c.stream, true, a);
 }
 
+// Workspace layout of one call: x images, x undo factors, split-K partials.
+struct TcLayout {
+    TcPlan plan;
+    int nb, kst;
+    size_t undo_off, part_off, total;
+};
+
+TcLayout LayoutTc(int M, int K, int N, int sms) {
+    TcLayout L;
+    L.nb = (K + 31) / 32;
+    L.kst = 2 * L.nb;  // stages of 16 elements
+    L.plan = PlanTc(M, N, L.nb, sms);
+    const size_t img_bytes = size_t(L.plan.mtiles) * L.kst * L.plan.mx * kTcK * 4;
+    L.undo_off = (img_bytes + 255) / 256 * 256;
+    L.part_off = L.undo_off + (size_t(M) * 4 + 255) / 256 * 256;
+    L.total = L.part_off + (L.plan.splits > 1 ? size_t(L.plan.splits) * M * N * 4 : 0);
+    return L;
+}
+
 template <int QT>
 void LaunchTcT(DeviceContext& c, const float* x, const uint8_t* w, int M, int K, int N, const float* bias,
-               float* y, int* status) {
-    const int nb = (K + 31) / 32;
-    const int kst = 2 * nb;  // stages of 16 elements
-    const TcPlan p = PlanTc(M, N, nb, c.sm_count);
-    const size_t img_bytes = size_t(p.mtiles) * kst * p.mx * kTcK * 4;
-    const size_t undo_off = (img_bytes + 255) / 256 * 256;
-    const size_t part_off = undo_off + (size_t(M) * 4 + 255) / 256 * 256;
-    const size_t part_bytes = p.splits > 1 ? size_t(p.splits) * M * N * 4 : 0;
-    uint8_t* ws = static_cast<uint8_t*>(Workspace(c, part_off + part_bytes));
+               float* y, int* status, void* workspace) {
+    const TcLayout L = LayoutTc(M, K, N, c.sm_count);
+    const TcPlan& p = L.plan;
+    const int nb = L.nb, kst = L.kst;
+    const size_t undo_off = L.undo_off, part_off = L.part_off;
+    uint8_t* ws = static_cast<uint8_t*>(workspace ? workspace : Workspace(c, L.total));
     float* undo = reinterpret_cast<float*>(ws + undo_off);
     float* part = reinterpret_cast<float*>(ws + part_off);
     Launch("TcPrepX", TcPrepX, dim3(p.mtiles * p.mx), dim3(128), 0, c.stream, true, x, M, K, p.mx, kst, undo, ws);
@@ -733,14 +749,16 @@ void LaunchTcT(DeviceContext& c, const float* x, const uint8_t* w, int M, int K,
 
 }  // namespace
 
+size_t TcWorkspaceBytes(int M, int K, int N, int sm_count) { return LayoutTc(M, K, N, sm_count).total; }
+
 void LaunchTcLinear(DeviceContext& c, int qtype, const float* x, const uint8_t* w, int M, int K, int N,
-                    const float* bias, float* y, int* status) {
+                    const float* bias, float* y, int* status, void* workspace) {
     static_assert(sizeof(TcShared) <= kTcHeader, "shared header");
     Require((reinterpret_cast<uintptr_t>(w) & 1) == 0, "mlb_quant_linear", "weight blocks must be 2-byte aligned");
     switch (qtype) {
-        case MLB_Q8_0: LaunchTcT<MLB_Q8_0>(c, x, w, M, K, N, bias, y, status); break;
-        case MLB_Q4_0: LaunchTcT<MLB_Q4_0>(c, x, w, M, K, N, bias, y, status); break;
-        default: LaunchTcT<MLB_Q4_1>(c, x, w, M, K, N, bias, y, status); break;
+        case MLB_Q8_0: LaunchTcT<MLB_Q8_0>(c, x, w, M, K, N, bias, y, status, workspace); break;
+        case MLB_Q4_0: LaunchTcT<MLB_Q4_0>(c, x, w, M, K, N, bias, y, status, workspace); break;
+        default: LaunchTcT<MLB_Q4_1>(c, x, w, M, K, N, bias, y, status, workspace); break;
     }
 }
 

@@ -193,3 +193,58 @@ class Session:
         if self.handle:
             self.lib.call("mlb_session_destroy", self.handle)
             self.handle = None
+
+
+def nccl_unique_id(lib: capi.Lib) -> bytes:
+    """A fresh NCCL id for one tensor-parallel group (mlb_nccl_unique_id)."""
+    buf = (ctypes.c_char * capi.NCCL_ID_BYTES)()
+    lib.call("mlb_nccl_unique_id", buf)
+    return bytes(buf)
+
+
+def batch_shard(lib: capi.Lib, spec: dict, tp_rank: int, tp_size: int) -> dict:
+    """The slices a tensor-parallel rank owns (mlb_batch_shard), as half-open
+    (begin, end) pairs: q heads, KV heads, dim rows, hidden rows, vocab rows."""
+    cfg = model_config(spec)
+    r = (ctypes.c_int * 10)()
+    lib.call("mlb_batch_shard", ctypes.byref(cfg), tp_rank, tp_size, r)
+    v = list(r)
+    return {"heads": (v[0], v[1]), "kv_heads": (v[2], v[3]), "dim": (v[4], v[5]),
+            "hidden": (v[6], v[7]), "vocab": (v[8], v[9])}
+
+
+class BatchSession:
+    """Lockstep greedy decoding of `batch` sequences (mlb_batch), optionally
+    tensor-parallel: every rank passes the same NCCL id (nccl_unique_id on one
+    rank, shared by the caller) and its own rank."""
+
+    def __init__(self, model: Model, batch: int, tp_rank: int = 0, tp_size: int = 1,
+                 nccl_id: bytes | None = None):
+        self.model, self.lib, self.batch = model, model.lib, batch
+        h = ctypes.c_void_p()
+        idbuf = ctypes.create_string_buffer(nccl_id, capi.NCCL_ID_BYTES) if nccl_id else None
+        self.lib.call("mlb_batch_create", model.handle, batch, tp_rank, tp_size, idbuf, ctypes.byref(h))
+        self.handle = h.value
+
+    def generate(self, prompts, n_new: int):
+        """prompts [batch, n_prompt] -> (tokens [batch, n_new], prefill_ms, decode_ms)."""
+        p = np.ascontiguousarray(prompts, dtype=np.int32)
+        assert p.ndim == 2 and p.shape[0] == self.batch
+        out = np.empty((self.batch, n_new), np.int32)
+        pre, dec = ctypes.c_float(), ctypes.c_float()
+        self.lib.call("mlb_batch_generate", self.handle, p.ctypes.data, p.shape[1], n_new, out.ctypes.data,
+                      ctypes.byref(pre), ctypes.byref(dec))
+        return out, pre.value, dec.value
+
+    def logits(self) -> np.ndarray:
+        """This rank's logits slice of the last step, [batch, cols]."""
+        ptr, cols, col0 = ctypes.c_void_p(), ctypes.c_int(), ctypes.c_int()
+        self.lib.call("mlb_batch_logits", self.handle, ctypes.byref(ptr), ctypes.byref(cols), ctypes.byref(col0))
+        out = np.empty((self.batch, cols.value), np.float32)
+        self.lib.call("mlb_memcpy_d2h", self.model.device, out.ctypes.data, ptr.value, out.nbytes)
+        return out
+
+    def close(self):
+        if self.handle:
+            self.lib.call("mlb_batch_destroy", self.handle)
+            self.handle = None
