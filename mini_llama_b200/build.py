@@ -69,7 +69,7 @@ def build(verbose: bool = False, force: bool = False) -> str:
         list(ex.map(run, jobs))
     if jobs or not os.path.exists(LIB):
         run([nvcc(), "-shared", "-gencode", "arch=compute_100a,code=sm_100a", "-o", LIB, *objs,
-             "-lcuda", "-lnccl"])
+             "-lcuda"])
     return LIB
 
 

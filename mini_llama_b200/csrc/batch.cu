@@ -23,6 +23,7 @@
 // A rank's slices are contiguous row ranges of the model's GGUF weights (a
 // pointer offset: no copy).  NCCL all-gathers concatenate rank-major
 // ([rank][b][slice]); GatherKernel reorders them into rows.
+#include <dlfcn.h>
 #include <nccl.h>
 
 #include <algorithm>
@@ -68,9 +69,44 @@ namespace {
 
 constexpr int kRowThreads = 256;
 
+// NCCL is opened on first use, not linked: a process that imports PyTorch
+// after loading this library must still resolve PyTorch's own NCCL, and most
+// uses of the library never need a collective.  An NCCL already loaded in
+// the process (PyTorch's) is reused; otherwise the system's libnccl.so.2.
+struct NcclApi {
+    ncclResult_t (*get_unique_id)(ncclUniqueId*) = nullptr;
+    ncclResult_t (*comm_init_rank)(ncclComm_t*, int, ncclUniqueId, int) = nullptr;
+    ncclResult_t (*all_gather)(const void*, void*, size_t, ncclDataType_t, ncclComm_t, cudaStream_t) = nullptr;
+    ncclResult_t (*comm_destroy)(ncclComm_t) = nullptr;
+    const char* (*error_string)(ncclResult_t) = nullptr;
+};
+
+const NcclApi& Nccl() {
+    static NcclApi api;
+    static bool loaded = false;
+    if (!loaded) {
+        void* h = dlopen("libnccl.so.2", RTLD_NOW | RTLD_NOLOAD);
+        if (!h) h = dlopen("libnccl.so.2", RTLD_NOW | RTLD_GLOBAL);
+        Require(h != nullptr, "NCCL", std::string("libnccl.so.2 could not be loaded: ") + dlerror(),
+                MLB_ERR_UNSUPPORTED);
+        auto sym = [&](const char* name) {
+            void* f = dlsym(h, name);
+            Require(f != nullptr, "NCCL", std::string("symbol missing: ") + name, MLB_ERR_UNSUPPORTED);
+            return f;
+        };
+        api.get_unique_id = reinterpret_cast<decltype(api.get_unique_id)>(sym("ncclGetUniqueId"));
+        api.comm_init_rank = reinterpret_cast<decltype(api.comm_init_rank)>(sym("ncclCommInitRank"));
+        api.all_gather = reinterpret_cast<decltype(api.all_gather)>(sym("ncclAllGather"));
+        api.comm_destroy = reinterpret_cast<decltype(api.comm_destroy)>(sym("ncclCommDestroy"));
+        api.error_string = reinterpret_cast<decltype(api.error_string)>(sym("ncclGetErrorString"));
+        loaded = true;
+    }
+    return api;
+}
+
 void CheckNccl(ncclResult_t r, const char* what) {
     if (r != ncclSuccess)
-        Fail(MLB_ERR_CUDA, std::string(what) + ": " + ncclGetErrorString(r));
+        Fail(MLB_ERR_CUDA, std::string(what) + ": " + Nccl().error_string(r));
 }
 
 __device__ __forceinline__ float BlockSumRow(float v, float* scratch) {
@@ -251,7 +287,7 @@ void CaptureBatchStep(mlb_batch* s, DeviceContext& c) {
     auto gather = [&](const float* local, int n_local, const float* add, float* dst) {
         const float* src = local;
         if (G > 1) {
-            CheckNccl(ncclAllGather(local, s->gbuf, size_t(B) * n_local, ncclFloat, s->comm, st), "ncclAllGather");
+            CheckNccl(Nccl().all_gather(local, s->gbuf, size_t(B) * n_local, ncclFloat, s->comm, st), "ncclAllGather");
             src = s->gbuf;
         }
         const size_t n = size_t(B) * G * n_local;
@@ -335,7 +371,7 @@ void CaptureBatchStep(mlb_batch* s, DeviceContext& c) {
                const_cast<const float*>(s->logits), vl, s->v0, s->pairs);
         const unsigned long long* all = s->pairs;
         if (G > 1) {
-            CheckNccl(ncclAllGather(s->pairs, s->pairs + B, size_t(B), ncclUint64, s->comm, st), "ncclAllGather");
+            CheckNccl(Nccl().all_gather(s->pairs, s->pairs + B, size_t(B), ncclUint64, s->comm, st), "ncclAllGather");
             all = s->pairs + B;
         }
         Launch("MergeArgmaxKernel", MergeArgmaxKernel, dim3(1), dim3(std::min(1024, std::max(32, B))), 0, st, true,
@@ -356,7 +392,7 @@ void DestroyBatch(mlb_batch* b) {
     if (b->graph) cudaGraphDestroy(b->graph);
     for (cudaEvent_t e : b->ev)
         if (e) cudaEventDestroy(e);
-    if (b->comm) ncclCommDestroy(b->comm);
+    if (b->comm) Nccl().comm_destroy(b->comm);
     for (void* p : b->allocations) cudaFree(p);
     delete b;
 }
@@ -372,8 +408,11 @@ int mlb_nccl_unique_id(void* id) {
     return Guard([&] {
         Require(id != nullptr, "mlb_nccl_unique_id", "null argument");
         static_assert(sizeof(ncclUniqueId) == MLB_NCCL_ID_BYTES, "NCCL id size");
+        int n = 0;
+        Require(cudaGetDeviceCount(&n) == cudaSuccess && n > 0, "mlb_nccl_unique_id", "no CUDA device",
+                MLB_ERR_UNSUPPORTED);
         ncclUniqueId u;
-        CheckNccl(ncclGetUniqueId(&u), "ncclGetUniqueId");
+        CheckNccl(Nccl().get_unique_id(&u), "ncclGetUniqueId");
         std::memcpy(id, &u, sizeof(u));
     });
 }
@@ -452,7 +491,7 @@ int mlb_batch_create(mlb_model* model, int batch, int tp_rank, int tp_size, cons
             if (tp_size > 1) {
                 ncclUniqueId id;
                 std::memcpy(&id, nccl_id, sizeof(id));
-                CheckNccl(ncclCommInitRank(&b->comm, tp_size, id, tp_rank), "ncclCommInitRank");
+                CheckNccl(Nccl().comm_init_rank(&b->comm, tp_size, id, tp_rank), "ncclCommInitRank");
             }
             CheckCuda(cudaDeviceSynchronize(), "cudaDeviceSynchronize");
             CaptureBatchStep(b, c);

@@ -166,6 +166,18 @@ __device__ __forceinline__ uint64_t GlobalTimerNs() {
     return t;
 }
 
+// One test of an mbarrier phase (no wait): true when it has completed.
+__device__ __forceinline__ bool MbarTryWait(uint64_t* bar, uint32_t parity) {
+    uint32_t done;
+    asm volatile(
+        "{\n .reg .pred p;\n mbarrier.test_wait.parity.shared::cta.b64 p, [%1], %2;\n"
+        " selp.u32 %0, 1, 0, p;\n}\n"
+        : "=r"(done)
+        : "r"(SmemAddr(bar)), "r"(parity)
+        : "memory");
+    return done != 0;
+}
+
 // Time-bounded wait on an mbarrier phase; also gives up when *abort becomes
 // nonzero (a shared flag another warp sets).  Returns false when it gave up.
 __device__ __forceinline__ bool MbarWaitFor(uint64_t* bar, uint32_t parity, uint64_t timeout_ns,

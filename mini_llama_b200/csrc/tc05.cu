@@ -537,17 +537,19 @@ __global__ void __launch_bounds__(kTcThreads, 1) TcLinearKernel(const TcArgs a) 
                 GridDepWait();  // the x images are the pre-pass's output
                 const uint32_t bytes = static_cast<uint32_t>(mx) * kTcK * 4;
                 int issued = 0;
+                int slot = (pass * nst) % xslots, use = (pass * nst) / xslots;
+                const uint8_t* src = a.ximg + (size_t(mt) * a.kst + 2 * kb0) * bytes;
                 for (int it = 0; it < nst; ++it) {
-                    const int git = pass * nst + it, slot = git % xslots, use = git / xslots;
-                    if (use > 0 && !MbarWaitFor(&sh.xempty[slot], (use - 1) & 1, kTcWaitNs, abort)) {
+                    if (use > 0 && !MbarTryWait(&sh.xempty[slot], (use - 1) & 1) &&
+                        !MbarWaitFor(&sh.xempty[slot], (use - 1) & 1, kTcWaitNs, abort)) {
                         if (!*abort) TcFail(sh, a.status);
                         break;
                     }
                     if (*abort) break;
                     MbarExpectTx(&sh.xfull[slot], bytes);
-                    BulkLoad(xring + size_t(slot) * bytes, a.ximg + (size_t(mt) * a.kst + 2 * kb0 + it) * bytes, bytes,
-                             &sh.xfull[slot]);
+                    BulkLoad(xring + size_t(slot) * bytes, src + size_t(it) * bytes, bytes, &sh.xfull[slot]);
                     issued = it + 1;
+                    if (++slot == xslots) slot = 0, ++use;
                 }
                 // copies still in flight land before the CTA moves on
                 for (int it = max(0, issued - xslots); it < issued; ++it) {
@@ -558,26 +560,35 @@ __global__ void __launch_bounds__(kTcThreads, 1) TcLinearKernel(const TcArgs a) 
             }
         } else {
             // ------------------------------------------------ MMA issue
+            // One thread runs this loop at dependent-instruction latency, so
+            // it keeps per-stage work minimal: descriptors are a base plus a
+            // slot offset (the 14-bit start-address field never carries),
+            // slots and phases advance by increments, and a completed barrier
+            // costs one try_wait.
             if (lane == 0) {
                 const uint32_t idesc = Idesc(mx);
-                const uint32_t xlbo = static_cast<uint32_t>(mx) * 16;
+                const uint64_t w0 = SmemDesc(SmemAddr(stages), kTcRows * 16);
+                const uint64_t x0 = SmemDesc(SmemAddr(xring), static_cast<uint32_t>(mx) * 16);
+                const uint64_t wstep = kTcStageBytes >> 4, wsub = kTcWBytes >> 4, wlo = kTcWImg >> 4;
+                const uint64_t xstep = static_cast<uint64_t>(4 * mx), xlo = static_cast<uint64_t>(2 * mx);
+                int slot = (pass * nst) % kTcStages, use = (pass * nst) / kTcStages;
+                int xs = (pass * nst) % xslots, xuse = (pass * nst) / xslots;
                 int last = -1;  // stage (of this pass) of the last commit
+                int lslot = 0, luse = 0;
                 for (int it = 0; it < nst; ++it) {
-                    const int git = pass * nst + it, slot = git % kTcStages, use = git / kTcStages;
-                    const int xs = git % xslots, xuse = git / xslots;
-                    if (!MbarWaitFor(&sh.xfull[xs], xuse & 1, kTcWaitNs, abort) ||
-                        !MbarWaitFor(&sh.wfull[slot], use & 1, kTcWaitNs, abort)) {
+                    if ((!MbarTryWait(&sh.xfull[xs], xuse & 1) &&
+                         !MbarWaitFor(&sh.xfull[xs], xuse & 1, kTcWaitNs, abort)) ||
+                        (!MbarTryWait(&sh.wfull[slot], use & 1) &&
+                         !MbarWaitFor(&sh.wfull[slot], use & 1, kTcWaitNs, abort))) {
                         if (!*abort) TcFail(sh, a.status);
                         break;
                     }
                     TcFenceAfter();
-                    const uint32_t sbase = SmemAddr(stages + size_t(slot) * kTcStageBytes);
-                    const uint32_t xb = SmemAddr(xring) + xs * (64 * mx);
-                    const uint64_t bhi = SmemDesc(xb, xlbo), blo = SmemDesc(xb + mx * kTcK * 2, xlbo);
+                    const uint64_t bhi = x0 + xs * xstep, blo = bhi + xlo;
+                    const uint64_t aw = w0 + slot * wstep;
 #pragma unroll
                     for (int t = 0; t < NW; ++t) {
-                        const uint32_t wb = sbase + t * kTcWBytes;
-                        const uint64_t ahi = SmemDesc(wb, kTcRows * 16), alo = SmemDesc(wb + kTcWImg, kTcRows * 16);
+                        const uint64_t ahi = aw + t * wsub, alo = ahi + wlo;
                         const uint32_t d = tmem + t * mx;
                         TcMma(d, ahi, bhi, idesc, it != 0);
                         TcMma(d, alo, bhi, idesc, 1);
@@ -586,14 +597,16 @@ __global__ void __launch_bounds__(kTcThreads, 1) TcLinearKernel(const TcArgs a) 
                     TcCommit(&sh.wempty[slot]);
                     TcCommit(&sh.xempty[xs]);
                     last = it;
+                    lslot = slot;
+                    luse = use;
+                    if (++slot == kTcStages) slot = 0, ++use;
+                    if (++xs == xslots) xs = 0, ++xuse;
                 }
                 if (last == nst - 1 && nst > 0) {
                     TcCommit(&sh.accfull);
                 } else if (last >= 0) {
                     // aborted: the MMAs issued so far finish before tensor memory is freed
-                    const int git = pass * nst + last;
-                    if (!MbarWaitFor(&sh.wempty[git % kTcStages], (git / kTcStages) & 1, kTcWaitNs, nullptr))
-                        TcFail(sh, a.status);
+                    if (!MbarWaitFor(&sh.wempty[lslot], luse & 1, kTcWaitNs, nullptr)) TcFail(sh, a.status);
                 }
             }
         }

@@ -72,3 +72,14 @@ def test_nccl_id_exchange_and_timing_max_over_gloo():
         res = dict(out)
     assert res[0][0] and res[1][0]
     assert res[0][1] == res[1][1] == [2.0, 10.0]
+
+
+def test_library_loaded_before_torch_leaves_torch_importable():
+    """NCCL is opened lazily: loading the library first must not bind a system
+    NCCL that PyTorch's own build cannot use."""
+    import subprocess
+    import sys
+    code = (f"import ctypes; ctypes.CDLL({capi.LIB_PATH!r}); import torch; "
+            "import torch.distributed; print('ok')")
+    r = subprocess.run([sys.executable, "-c", code], capture_output=True, text=True, timeout=300)
+    assert r.returncode == 0 and r.stdout.strip().endswith("ok"), r.stderr[-2000:]
