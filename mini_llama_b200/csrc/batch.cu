@@ -87,8 +87,10 @@ const NcclApi& Nccl() {
     if (!loaded) {
         void* h = dlopen("libnccl.so.2", RTLD_NOW | RTLD_NOLOAD);
         if (!h) h = dlopen("libnccl.so.2", RTLD_NOW | RTLD_GLOBAL);
-        Require(h != nullptr, "NCCL", std::string("libnccl.so.2 could not be loaded: ") + dlerror(),
-                MLB_ERR_UNSUPPORTED);
+        if (!h) {
+            const char* e = dlerror();
+            Fail(MLB_ERR_UNSUPPORTED, std::string("NCCL: libnccl.so.2 could not be loaded: ") + (e ? e : "unknown"));
+        }
         auto sym = [&](const char* name) {
             void* f = dlsym(h, name);
             Require(f != nullptr, "NCCL", std::string("symbol missing: ") + name, MLB_ERR_UNSUPPORTED);
