@@ -42,6 +42,12 @@ __device__ __forceinline__ void RedAdd(float* p, float v) {
     asm volatile("red.global.add.f32 [%0], %1;" ::"l"(p), "f"(v) : "memory");
 }
 
+// Four consecutive floats in one 16-byte vector reduction (p 16-byte aligned).
+__device__ __forceinline__ void RedAdd4(float* p, float4 v) {
+    asm volatile("red.global.add.v4.f32 [%0], {%1, %2, %3, %4};" ::"l"(p), "f"(v.x), "f"(v.y), "f"(v.z), "f"(v.w)
+                 : "memory");
+}
+
 __host__ __device__ constexpr size_t Round128(size_t b) { return (b + 127) & ~size_t(127); }
 
 struct Chunk {  // one ring stage of the schedule: one or two bulk copies, back to back
@@ -546,9 +552,18 @@ __device__ __forceinline__ void ColumnDotSmem(const LaneMma L, const uint8_t* co
 // After a barrier: out[i] += acc[i] (+ addend[i]) for i < n by red.add, one
 // coalesced pass, and acc back to zero.
 __device__ __forceinline__ void FlushRed(float* acc, float* out, int n, const float* addend) {
-    for (int i = threadIdx.x; i < n; i += 256) {
-        RedAdd(out + i, acc[i] + (addend ? __ldcg(addend + i) : 0.0f));
-        acc[i] = 0.0f;
+    // n is a multiple of 32; acc (shared), out and addend are 16-byte aligned
+    for (int i = 4 * threadIdx.x; i < n; i += 4 * 256) {
+        float4 a = *reinterpret_cast<const float4*>(acc + i);
+        if (addend) {
+            const float4 b = __ldcg(reinterpret_cast<const float4*>(addend + i));
+            a.x += b.x;
+            a.y += b.y;
+            a.z += b.z;
+            a.w += b.w;
+        }
+        RedAdd4(out + i, a);
+        *reinterpret_cast<float4*>(acc + i) = make_float4(0.f, 0.f, 0.f, 0.f);
     }
 }
 
