@@ -27,6 +27,11 @@
 // (leading byte offset 16 R between the two 8-element k chunks, stride byte
 // offset 128 between 8-row groups).
 //
+// Batches of up to 128 rows may instead run with the roles swapped: A = the x
+// tile padded to 128 rows, B = 256 W rows in one image, so a stage takes three
+// 128 x 256 MMAs rather than six narrow ones (tcgen05.mma issue, about 95
+// cycles each, bounds the narrow form).  The planner picks by a cycle model.
+//
 // A CTA owns NW x 128 W rows (NW = 1 or 2) and MX x rows over a range of K
 // (split-K when the tile grid alone would leave SMs idle); its NW accumulators
 // of 128 x MX fp32 fill up to all 512 tensor-memory columns.  One stage is 16
@@ -363,8 +368,12 @@ __device__ __forceinline__ void TcFail(TcShared& sh, int* status) {
     *reinterpret_cast<volatile int*>(&sh.abort) = 1;
 }
 
-template <int QT, int NW>
+// SW (swapped roles, small batches): NW == 2, A = the x tile padded to 128
+// rows (MX == 128), B = the CTA's 256 W rows as one image, one 128 x 256
+// accumulator; three MMAs per stage instead of six.
+template <int QT, int NW, bool SW>
 __global__ void __launch_bounds__(kTcThreads, 1) TcLinearKernel(const TcArgs a) {
+    static_assert(!SW || NW == 2, "the swapped form covers 256 W rows");
     extern __shared__ __align__(1024) uint8_t smem[];
     TcShared& sh = *reinterpret_cast<TcShared*>(smem);
     uint8_t* stages = smem + kTcHeader;
@@ -404,7 +413,7 @@ __global__ void __launch_bounds__(kTcThreads, 1) TcLinearKernel(const TcArgs a) 
     }
     if (tid < 2 * kTcRows) sh.wundo[tid] = 1.0f;
     uint32_t ncols = 32;
-    while (ncols < static_cast<uint32_t>(NW * mx)) ncols <<= 1;
+    while (ncols < static_cast<uint32_t>(SW ? 2 * kTcRows : NW * mx)) ncols <<= 1;
     if (warp == kTcDqWarps + 1) {
         asm volatile("tcgen05.alloc.cta_group::1.sync.aligned.shared::cta.b32 [%0], %1;" ::"r"(SmemAddr(&sh.tmem)),
                      "r"(ncols));
@@ -505,9 +514,11 @@ __global__ void __launch_bounds__(kTcThreads, 1) TcLinearKernel(const TcArgs a) 
                             uint4 hi, lo;
                             TcConvert<QT>(r, h, mul[i], hi, lo);
                             const int row = rb + kTcRows * i, t = row >> 7, rr = row & 127;
-                            uint8_t* dst = st + t * kTcWBytes + c * (kTcRows * 16) + (rr >> 3) * 128 + (rr & 7) * 16;
+                            // SW: one 256-row hi image, then the lo image
+                            uint8_t* dst = SW ? st + c * (2 * kTcRows * 16) + (row >> 3) * 128 + (row & 7) * 16
+                                              : st + t * kTcWBytes + c * (kTcRows * 16) + (rr >> 3) * 128 + (rr & 7) * 16;
                             *reinterpret_cast<uint4*>(dst) = hi;
-                            *reinterpret_cast<uint4*>(dst + kTcWImg) = lo;
+                            *reinterpret_cast<uint4*>(dst + (SW ? 2 * kTcWImg : kTcWImg)) = lo;
                         }
                         asm volatile("fence.proxy.async.shared::cta;" ::: "memory");
                         __syncwarp();
@@ -566,8 +577,8 @@ __global__ void __launch_bounds__(kTcThreads, 1) TcLinearKernel(const TcArgs a) 
             // slots and phases advance by increments, and a completed barrier
             // costs one try_wait.
             if (lane == 0) {
-                const uint32_t idesc = Idesc(mx);
-                const uint64_t w0 = SmemDesc(SmemAddr(stages), kTcRows * 16);
+                const uint32_t idesc = Idesc(SW ? 2 * kTcRows : mx);
+                const uint64_t w0 = SmemDesc(SmemAddr(stages), (SW ? 2 : 1) * kTcRows * 16);
                 const uint64_t x0 = SmemDesc(SmemAddr(xring), static_cast<uint32_t>(mx) * 16);
                 const uint64_t wstep = kTcStageBytes >> 4, wsub = kTcWBytes >> 4, wlo = kTcWImg >> 4;
                 const uint64_t xstep = static_cast<uint64_t>(4 * mx), xlo = static_cast<uint64_t>(2 * mx);
@@ -584,15 +595,22 @@ __global__ void __launch_bounds__(kTcThreads, 1) TcLinearKernel(const TcArgs a) 
                         break;
                     }
                     TcFenceAfter();
-                    const uint64_t bhi = x0 + xs * xstep, blo = bhi + xlo;
+                    const uint64_t xhi = x0 + xs * xstep, xlo2 = xhi + xlo;
                     const uint64_t aw = w0 + slot * wstep;
+                    if constexpr (SW) {  // A = x (128 rows), B = W (256 rows)
+                        const uint64_t whi = aw, wlo2 = aw + 2 * wlo;
+                        TcMma(tmem, xhi, whi, idesc, it != 0);
+                        TcMma(tmem, xhi, wlo2, idesc, 1);
+                        TcMma(tmem, xlo2, whi, idesc, 1);
+                    } else {  // A = W (128 rows per sub-tile), B = x (MX rows)
 #pragma unroll
-                    for (int t = 0; t < NW; ++t) {
-                        const uint64_t ahi = aw + t * wsub, alo = ahi + wlo;
-                        const uint32_t d = tmem + t * mx;
-                        TcMma(d, ahi, bhi, idesc, it != 0);
-                        TcMma(d, alo, bhi, idesc, 1);
-                        TcMma(d, ahi, blo, idesc, 1);
+                        for (int t = 0; t < NW; ++t) {
+                            const uint64_t ahi = aw + t * wsub, alo = ahi + wlo;
+                            const uint32_t d = tmem + t * mx;
+                            TcMma(d, ahi, xhi, idesc, it != 0);
+                            TcMma(d, alo, xhi, idesc, 1);
+                            TcMma(d, ahi, xlo2, idesc, 1);
+                        }
                     }
                     TcCommit(&sh.wempty[slot]);
                     TcCommit(&sh.xempty[xs]);
@@ -637,7 +655,34 @@ __global__ void __launch_bounds__(kTcThreads, 1) TcLinearKernel(const TcArgs a) 
         bool ok = MbarWaitFor(&sh.accfull, pass & 1, kTcWaitNs, abort);
         if (!ok && !*abort) TcFail(sh, a.status);
         TcFenceAfter();
-        if (ok && !*abort) {
+        if (ok && !*abort && SW) {
+            // lanes = x rows, columns = W rows (half 0: 0..127, half 1: 128..255)
+            const int q = warp & 3, half = warp >> 2;
+            const int m = m0 + 32 * q + lane;
+            const float xu = m < a.M ? __ldg(a.xundo + m) : 0.0f;
+            float* dst = (a.splits == 1 ? a.y : a.part + size_t(split) * a.M * a.N) + size_t(m < a.M ? m : 0) * a.N;
+            const bool vec = (a.N & 3) == 0;
+            for (int col = half * kTcRows; col < (half + 1) * kTcRows; col += 8) {
+                float v[8];
+                TcLoad8(tmem + (static_cast<uint32_t>(32 * q) << 16) + col, v);
+                if (m >= a.M) continue;
+                const int nb = n0 + col;
+                float out[8];
+#pragma unroll
+                for (int i = 0; i < 8; ++i) {
+                    const int n = nb + i;
+                    out[i] = n < a.N ? v[i] * xu * sh.wundo[col + i] + ((a.splits == 1 && a.bias) ? a.bias[n] : 0.0f)
+                                     : 0.0f;
+                }
+                if (vec && nb + 8 <= a.N) {
+                    reinterpret_cast<float4*>(dst + nb)[0] = make_float4(out[0], out[1], out[2], out[3]);
+                    reinterpret_cast<float4*>(dst + nb)[1] = make_float4(out[4], out[5], out[6], out[7]);
+                } else {
+                    for (int i = 0; i < 8; ++i)
+                        if (nb + i < a.N) dst[nb + i] = out[i];
+                }
+            }
+        } else if (ok && !*abort) {
             const int q = warp & 3, half = warp >> 2;
             const int t = NW == 2 ? half : 0;
             const int r = 32 * q + lane, n = n0 + t * kTcRows + r;
@@ -667,6 +712,7 @@ __global__ void __launch_bounds__(kTcThreads, 1) TcLinearKernel(const TcArgs a) 
 // ---------------------------------------------------------------- host plan
 struct TcPlan {
     int nw, mx, mtiles, kper, splits;
+    bool sw;  // swapped roles: A = x (128 rows), B = 256 W rows
 };
 
 // Tile shape and split-K from a cost model in SM cycles: per 32-element block
@@ -676,46 +722,60 @@ struct TcPlan {
 // epilogue, times the waves of CTAs over the SMs, plus the partial-sum pass
 // when K is split.
 TcPlan PlanTc(int M, int N, int nb, int sms) {
-    TcPlan best{2, 16, 1, nb, 1};
+    TcPlan best{2, 16, 1, nb, 1, false};
     double best_t = 1e300;
+    auto consider = [&](int nw, int mx, int mtiles, bool sw, double block) {
+        const long long ntiles = (N + nw * kTcRows - 1) / (nw * kTcRows);
+        for (int s = 1; s <= std::min(nb, 32); ++s) {
+            const int kper = (nb + s - 1) / s;
+            const int splits = (nb + kper - 1) / kper;
+            if (splits != s) continue;
+            const long long ctas = ntiles * mtiles * splits;
+            const long long waves = (ctas + sms - 1) / sms;
+            double t = double(waves) * (3000.0 + kper * block + 12.0 * nw * mx);
+            if (splits > 1) t += 2000.0 + double(M) * N * 4.0 * (splits + 1) / (23.5 * sms);
+            if (t < best_t) {
+                best_t = t;
+                best = TcPlan{nw, mx, mtiles, kper, splits, sw};
+            }
+        }
+    };
+    // per-block cycles: the MMA thread (~160 a tcgen05.mma with its share of
+    // the stage's waits and commits, measured), tensor time, shared-memory
+    // wavefronts (operand reads, images, raw ring) and the HBM share of W
+    constexpr double kMmaCycles = 160.0;
+    if (M <= kTcRows) {
+        const double smem_bytes = 2.0 * (3.0 * (kTcWImg + 2.0 * kTcWImg) + kTcWBytes * 2.0 + kTcRows * kTcK * 4.0) +
+                                  2.0 * 2 * kTcRows * 48.0;
+        const double block = std::max({2 * 3 * kMmaCycles, 2 * 3 * 128.0, smem_bytes / 128.0, 380.0}) + 150.0;
+        consider(2, kTcRows, 1, true, block);
+    }
     const int mt_min = (M + kTcMaxX - 1) / kTcMaxX;
     for (int nw = 1; nw <= 2; ++nw) {
-        const long long ntiles = (N + nw * kTcRows - 1) / (nw * kTcRows);
         for (int mtiles = mt_min; mtiles <= mt_min + 3; ++mtiles) {
             const int mx = ((M + mtiles - 1) / mtiles + 15) / 16 * 16;
             if (mx > kTcMaxX || (mtiles > mt_min && mx < 64)) continue;
             const double smem_bytes = 2.0 * nw * (3.0 * (kTcWImg + 2.0 * kTcK * mx) + kTcWBytes) +
                                       2.0 * nw * kTcRows * 48.0;
-            const double block = std::max({3.0 * nw * mx, smem_bytes / 128.0, 190.0 * nw}) + 150.0;
-            for (int s = 1; s <= std::min(nb, 32); ++s) {
-                const int kper = (nb + s - 1) / s;
-                const int splits = (nb + kper - 1) / kper;
-                if (splits != s) continue;
-                const long long ctas = ntiles * mtiles * splits;
-                const long long waves = (ctas + sms - 1) / sms;
-                double t = double(waves) * (3000.0 + kper * block + 12.0 * nw * mx);
-                if (splits > 1) t += 2000.0 + double(M) * N * 4.0 * (splits + 1) / (23.5 * sms);
-                if (t < best_t) {
-                    best_t = t;
-                    best = TcPlan{nw, mx, mtiles, kper, splits};
-                }
-            }
+            const double block =
+                std::max({2 * 3 * kMmaCycles * nw, 3.0 * nw * mx, smem_bytes / 128.0, 190.0 * nw}) + 150.0;
+            consider(nw, mx, mtiles, false, block);
         }
     }
     return best;
 }
 
-template <int QT, int NW>
+template <int QT, int NW, bool SW>
 void LaunchTcKernel(DeviceContext& c, dim3 grid, const TcArgs& a) {
     constexpr size_t smem = TcSmemBytes<QT>();
     static int configured[64] = {};
     if (c.device >= 64 || !configured[c.device]) {
-        CheckCuda(cudaFuncSetAttribute(TcLinearKernel<QT, NW>, cudaFuncAttributeMaxDynamicSharedMemorySize,
+        CheckCuda(cudaFuncSetAttribute(TcLinearKernel<QT, NW, SW>, cudaFuncAttributeMaxDynamicSharedMemorySize,
                                        static_cast<int>(smem)),
                   "cudaFuncSetAttribute(TcLinearKernel)");
         if (c.device < 64) configured[c.device] = 1;
     }
-    Launch("TcLinearKernel", TcLinearKernel<QT, NW>, grid, dim3(kTcThreads), smem, c.stream, true, a);
+    Launch("TcLinearKernel", TcLinearKernel<QT, NW, SW>, grid, dim3(kTcThreads), smem, c.stream, true, a);
 }
 
 // Workspace layout of one call: x images, x undo factors, split-K partials.
@@ -750,8 +810,9 @@ void LaunchTcT(DeviceContext& c, const float* x, const uint8_t* w, int M, int K,
     Launch("TcPrepX", TcPrepX, dim3(p.mtiles * p.mx), dim3(128), 0, c.stream, true, x, M, K, p.mx, kst, undo, ws);
     TcArgs a{w, N, K, nb, M, p.mx, p.mtiles, kst, p.kper, ws, undo, bias, y, part, p.splits, status};
     const dim3 grid(p.mtiles * p.splits, (N + p.nw * kTcRows - 1) / (p.nw * kTcRows));
-    if (p.nw == 2) LaunchTcKernel<QT, 2>(c, grid, a);
-    else LaunchTcKernel<QT, 1>(c, grid, a);
+    if (p.sw) LaunchTcKernel<QT, 2, true>(c, grid, a);
+    else if (p.nw == 2) LaunchTcKernel<QT, 2, false>(c, grid, a);
+    else LaunchTcKernel<QT, 1, false>(c, grid, a);
     if (p.splits > 1) {
         const size_t mn = size_t(M) * N;
         const int g = static_cast<int>(std::min<size_t>((mn + 255) / 256, size_t(8) * c.sm_count));
