@@ -55,8 +55,11 @@
 // Every wait is bounded (an expired wait records MLB_ERR_DEVICE_TIMEOUT and
 // raises the CTA's abort flag); in-flight copies and MMAs are waited for and
 // tensor memory is freed on every path.
+#include <cuda.h>
+
 #include <algorithm>
 #include <cmath>
+#include <cstring>
 
 #include "common.cuh"
 #include "qgemv.cuh"
@@ -361,7 +364,16 @@ struct TcArgs {
     float* part;  // splits > 1: [splits][M][N]
     int splits;
     int* status;
+    int tma_rows;  // 0: one bulk copy per row; else P: the tensor map views P rows as one
 };
+
+// One 2-D tensor-map box (no multicast) into shared memory, completing on bar.
+__device__ __forceinline__ void TmaLoad2D(void* dst, const CUtensorMap* map, int x, int y, uint64_t* bar) {
+    asm volatile(
+        "cp.async.bulk.tensor.2d.shared::cluster.global.mbarrier::complete_tx::bytes [%0], [%1, {%2, %3}], [%4];"
+        ::"r"(SmemAddr(dst)), "l"(reinterpret_cast<uint64_t>(map)), "r"(x), "r"(y), "r"(SmemAddr(bar))
+        : "memory");
+}
 
 __device__ __forceinline__ void TcFail(TcShared& sh, int* status) {
     atomicCAS(status, 0, MLB_ERR_DEVICE_TIMEOUT);
@@ -372,7 +384,7 @@ __device__ __forceinline__ void TcFail(TcShared& sh, int* status) {
 // rows (MX == 128), B = the CTA's 256 W rows as one image, one 128 x 256
 // accumulator; three MMAs per stage instead of six.
 template <int QT, int NW, bool SW>
-__global__ void __launch_bounds__(kTcThreads, 1) TcLinearKernel(const TcArgs a) {
+__global__ void __launch_bounds__(kTcThreads, 1) TcLinearKernel(const TcArgs a, const __grid_constant__ CUtensorMap wmap) {
     static_assert(!SW || NW == 2, "the swapped form covers 256 W rows");
     extern __shared__ __align__(1024) uint8_t smem[];
     TcShared& sh = *reinterpret_cast<TcShared*>(smem);
@@ -403,7 +415,8 @@ __global__ void __launch_bounds__(kTcThreads, 1) TcLinearKernel(const TcArgs a) 
             MbarInit(&sh.xempty[i], 1);
         }
         for (int i = 0; i < kTcRawSlots; ++i) {
-            MbarInit(&sh.rawfull[i], kTcDqWarps);  // + the bytes of the warps' bulk copies
+            // one arrival per warp with its rows' bulk copies, or one for the tensor-map boxes
+            MbarInit(&sh.rawfull[i], a.tma_rows ? 1 : kTcDqWarps);
             MbarInit(&sh.rawempty[i], kTcDqWarps);
         }
         MbarInit(&sh.accfull, 1);
@@ -454,6 +467,17 @@ __global__ void __launch_bounds__(kTcThreads, 1) TcLinearKernel(const TcArgs a) 
                 if (gw >= kTcRawSlots &&
                     !MbarWaitFor(&sh.rawempty[rs], (gw / kTcRawSlots - 1) & 1, kTcWaitNs, abort))
                     return false;
+                if (a.tma_rows) {  // P boxes of (NW x 128 / P rows, kRawRow bytes): row P i + j -> box j, row i
+                    if (tid == 0) {
+                        const int P = a.tma_rows, rows = NW * kTcRows / P;
+                        const long long k0 = (long long)(kb0 + wi * TcBlock<QT>::kWin) * kBB;
+                        MbarExpectTx(&sh.rawfull[rs], static_cast<uint32_t>(NW * kTcRows * kRawRow));
+                        for (int j = 0; j < P; ++j)
+                            TmaLoad2D(raw + rs * kRawSlot + j * rows * kRawRow, &wmap,
+                                      static_cast<int>((j * (long long)rowbytes + k0) & ~15LL), n0 / P, &sh.rawfull[rs]);
+                    }
+                    return true;
+                }
                 uint32_t bytes = 0;
                 if (tid < NW * kTcRows) {
                     const int n = n0 + tid, b0 = wi * TcBlock<QT>::kWin;
@@ -494,7 +518,9 @@ __global__ void __launch_bounds__(kTcThreads, 1) TcLinearKernel(const TcArgs a) 
 #pragma unroll
                 for (int i = 0; i < kItems; ++i) {
                     const uintptr_t src = reinterpret_cast<uintptr_t>(rowp[i]) + size_t(kb0 + b0) * kBB;
-                    rowbase[i] = rbase + (rb + kTcRows * i) * kRawRow + static_cast<uint32_t>(src & 15);
+                    const int r = rb + kTcRows * i;
+                    const int roff = a.tma_rows ? (r % a.tma_rows) * (NW * kTcRows / a.tma_rows) + r / a.tma_rows : r;
+                    rowbase[i] = rbase + roff * kRawRow + static_cast<uint32_t>(src & 15);
                 }
                 bool big = false;
                 for (int j = 0; j < nblk && ok; ++j) {
@@ -765,8 +791,31 @@ TcPlan PlanTc(int M, int N, int nb, int sms) {
     return best;
 }
 
+// The weight blocks as a 2-D tensor map for the raw-window copies: rows viewed
+// P at a time (P the smallest of 1, 2, 4, 8 that makes the row stride a
+// multiple of 16 bytes), boxes of kRawRow bytes x (cta_rows / P) rows.
+// Returns P, or 0 (per-row bulk copies) when the rows do not divide into
+// such groups or the base is not 16-byte aligned.
+template <int QT>
+int WeightMap(const uint8_t* w, int N, int nb, int cta_rows, CUtensorMap& map) {
+    std::memset(&map, 0, sizeof(map));
+    const size_t rowbytes = size_t(nb) * TcBlock<QT>::kBytes;
+    int P = 1;
+    while (P <= 8 && (P * rowbytes) % 16 != 0) P *= 2;
+    if (P > 8 || N % P != 0 || (reinterpret_cast<uintptr_t>(w) & 15) != 0 || cta_rows / P > 256) return 0;
+    const cuuint64_t gdim[2] = {cuuint64_t(P * rowbytes), cuuint64_t(N / P)};
+    const cuuint64_t gstride[1] = {cuuint64_t(P * rowbytes)};
+    const cuuint32_t box[2] = {cuuint32_t(TcBlock<QT>::kRawRow), cuuint32_t(cta_rows / P)};
+    const cuuint32_t estride[2] = {1, 1};
+    const CUresult r = cuTensorMapEncodeTiled(&map, CU_TENSOR_MAP_DATA_TYPE_UINT8, 2, const_cast<uint8_t*>(w), gdim,
+                                              gstride, box, estride, CU_TENSOR_MAP_INTERLEAVE_NONE,
+                                              CU_TENSOR_MAP_SWIZZLE_NONE, CU_TENSOR_MAP_L2_PROMOTION_L2_256B,
+                                              CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
+    return r == CUDA_SUCCESS ? P : 0;
+}
+
 template <int QT, int NW, bool SW>
-void LaunchTcKernel(DeviceContext& c, dim3 grid, const TcArgs& a) {
+void LaunchTcKernel(DeviceContext& c, dim3 grid, const TcArgs& a, const CUtensorMap& wmap) {
     constexpr size_t smem = TcSmemBytes<QT>();
     static int configured[64] = {};
     if (c.device >= 64 || !configured[c.device]) {
@@ -775,7 +824,7 @@ void LaunchTcKernel(DeviceContext& c, dim3 grid, const TcArgs& a) {
                   "cudaFuncSetAttribute(TcLinearKernel)");
         if (c.device < 64) configured[c.device] = 1;
     }
-    Launch("TcLinearKernel", TcLinearKernel<QT, NW, SW>, grid, dim3(kTcThreads), smem, c.stream, true, a);
+    Launch("TcLinearKernel", TcLinearKernel<QT, NW, SW>, grid, dim3(kTcThreads), smem, c.stream, true, a, wmap);
 }
 
 // Workspace layout of one call: x images, x undo factors, split-K partials.
@@ -808,11 +857,13 @@ void LaunchTcT(DeviceContext& c, const float* x, const uint8_t* w, int M, int K,
     float* undo = reinterpret_cast<float*>(ws + undo_off);
     float* part = reinterpret_cast<float*>(ws + part_off);
     Launch("TcPrepX", TcPrepX, dim3(p.mtiles * p.mx), dim3(128), 0, c.stream, true, x, M, K, p.mx, kst, undo, ws);
-    TcArgs a{w, N, K, nb, M, p.mx, p.mtiles, kst, p.kper, ws, undo, bias, y, part, p.splits, status};
+    TcArgs a{w, N, K, nb, M, p.mx, p.mtiles, kst, p.kper, ws, undo, bias, y, part, p.splits, status, 0};
     const dim3 grid(p.mtiles * p.splits, (N + p.nw * kTcRows - 1) / (p.nw * kTcRows));
-    if (p.sw) LaunchTcKernel<QT, 2, true>(c, grid, a);
-    else if (p.nw == 2) LaunchTcKernel<QT, 2, false>(c, grid, a);
-    else LaunchTcKernel<QT, 1, false>(c, grid, a);
+    CUtensorMap wmap;
+    a.tma_rows = WeightMap<QT>(w, N, nb, p.nw * kTcRows, wmap);
+    if (p.sw) LaunchTcKernel<QT, 2, true>(c, grid, a, wmap);
+    else if (p.nw == 2) LaunchTcKernel<QT, 2, false>(c, grid, a, wmap);
+    else LaunchTcKernel<QT, 1, false>(c, grid, a, wmap);
     if (p.splits > 1) {
         const size_t mn = size_t(M) * N;
         const int g = static_cast<int>(std::min<size_t>((mn + 255) / 256, size_t(8) * c.sm_count));
