@@ -793,6 +793,7 @@ __device__ unsigned Consumers(const MegaParams& p, const MkSmem& s) {
                     (part == 0 ? q : (part == 1 ? kn : vn))[d] = __uint_as_float(static_cast<unsigned>(wv));
                 }
                 for (int i = tid; i < hd; i += 256) o[i] = 0.0f;
+                CpAsyncWaitAll();  // this thread's RoPE-table copies; the barrier publishes them
                 ConsumerBar();
                 if (tid == 0) s.flags[4] = s.flags[0] == 0;
                 ConsumerBar();
