@@ -338,7 +338,8 @@ def run_ours(args):
         "warmup": args.warmup, "ms_per_step": secs / args.steps * 1e3, "higher_is_better": True,
         "scaling": "weak", "vs_baseline": None, "dtype": "f32 activations, Q8_0 weights",
         "data": "synthetic (seeded random-init weights and prompt ids)",
-        "config": dict(CONFIG, parallelism=f"replicas x{world}" if world > 1 else "single GPU"),
+        "config": dict(CONFIG, global_batch=world,  # one independent sequence per GPU
+                       parallelism=f"replicas x{world}" if world > 1 else "single GPU"),
         "e2e": {"value": e2e, "unit": UNIT, "h2d_bytes_per_step": 4 + 8 + 4,
                 "d2h_bytes_per_step": NEW * 4 + 4,
                 "path": "mlb_session_generate(host start token -> host 128 token ids)"},
