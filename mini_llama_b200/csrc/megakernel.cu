@@ -599,9 +599,26 @@ __device__ __forceinline__ void DigitsWarp(float v, int8_t* dblk, int dstride, f
 // CTAs per attention head: one per wo block column when every head can have
 // that many, so each CTA of a head runs the head's attention and projects
 // through its own column; else one CTA per head and all its columns.
-__host__ __device__ __forceinline__ int HeadSplit(const MegaParams& p, int G) {
+struct AttnPlan {
+    int hsplit;  // CTAs per head over its wo block columns (1 or hd / 32)
+    int rsplit;  // and over the rows of each column (1 or 2)
+    int items;   // n_heads x hsplit x rsplit
+};
+
+__host__ __device__ __forceinline__ AttnPlan AttnSplit(const MegaParams& p, int G) {
     const int bph = p.hd / 32;
-    return p.n_heads * bph <= G ? bph : 1;
+    AttnPlan a;
+    a.hsplit = p.n_heads * bph <= G ? bph : 1;
+    a.rsplit = (a.hsplit == bph && 2 * p.n_heads * bph <= G && (p.dim + 15) / 16 >= 2) ? 2 : 1;
+    a.items = p.n_heads * a.hsplit * a.rsplit;
+    return a;
+}
+
+// Row tiles [t0, t1) of the wo block column that part rh of rsplit projects.
+__host__ __device__ __forceinline__ void AttnRows(int ntiles, int rsplit, int rh, int& t0, int& t1) {
+    const int per = (ntiles + rsplit - 1) / rsplit;
+    t0 = rh * per < ntiles ? rh * per : ntiles;
+    t1 = t0 + per < ntiles ? t0 + per : ntiles;
 }
 
 
@@ -616,7 +633,7 @@ __device__ void ForEachChunk(const MegaParams& p, int c, int G, F&& f) {
     const int nj = p.hidden / 32;
     const int t_lm = (p.vocab + 15) / 16;
     const int bph = p.hd / 32;  // wo block columns per head
-    const int hsplit = HeadSplit(p, G);
+    const AttnPlan ap = AttnSplit(p, G);
     for (int l = 0; l < p.n_layers; ++l) {
         const MegaLayer& L = p.layers[l];
         for (int t = c; t < t_qkv; t += G) {
@@ -624,9 +641,16 @@ __device__ void ForEachChunk(const MegaParams& p, int c, int G, F&& f) {
             const int ti = seg == 0 ? t : (seg == 1 ? t - tq : t - tq - tk);
             f(Chunk{L.wqkv[seg] + size_t(ti) * tile_b, nullptr, tile_b, 0});
         }
-        for (int it = G - 1 - c; it < p.n_heads * hsplit; it += G)  // attention items (head, its wo columns)
-            for (int j = (it % hsplit) * (bph / hsplit); j < (it % hsplit + 1) * (bph / hsplit); ++j)
-                f(Chunk{L.wo + size_t((it / hsplit) * bph + j) * col_b, nullptr, col_b, 0});
+        // attention items (head, its wo columns, a row range of them)
+        for (int it = G - 1 - c; it < ap.items; it += G) {
+            const int per_head = ap.hsplit * ap.rsplit, rem = it % per_head, h = it / per_head;
+            const int ci = rem / ap.rsplit, rh = rem % ap.rsplit;
+            int t0, t1;
+            AttnRows(ntiles_dim, ap.rsplit, rh, t0, t1);
+            for (int j = ci * (bph / ap.hsplit); j < (ci + 1) * (bph / ap.hsplit); ++j)
+                f(Chunk{L.wo + size_t(h * bph + j) * col_b + size_t(t0) * kR16Chunk, nullptr,
+                        static_cast<uint32_t>(t1 - t0) * kR16Chunk, 0});
+        }
         // FFN: per 32-unit hidden block j, its gate rows, its up rows, its
         // w_down block column (R16C)
         for (int j = c; j < nj; j += G) {
@@ -657,8 +681,8 @@ __device__ unsigned Consumers(const MegaParams& p, const MkSmem& s) {
     const int bph = p.hd / 32;
     // signals per step: one per QKV worker CTA, one per head, one per FFN
     // worker CTA; every CTA takes one LM ticket
-    const int hsplit = HeadSplit(p, G);
-    const unsigned w_att = p.n_heads * hsplit, w_ffn = WorkerCount(G, nj), w_lm = G;
+    const AttnPlan ap = AttnSplit(p, G);
+    const unsigned w_att = ap.items, w_ffn = WorkerCount(G, nj), w_lm = G;
     const int ctr_lm_ticket = kMkPhases * p.n_layers, ctr_token = kMkPhases * p.n_layers + 1;
     Ring rg;  // the chunk sequence thread 0 issued in the prologue, continued here
     rg.n = 0;
@@ -737,8 +761,13 @@ __device__ unsigned Consumers(const MegaParams& p, const MkSmem& s) {
                 Trace(p, step, l, 1);
             }
             // ---------------- attention + O projection, one query head
-            for (int it = G - 1 - c; it < p.n_heads * hsplit; it += G) {
-                const int h = it / hsplit, j0 = (it % hsplit) * (bph / hsplit), j1 = j0 + bph / hsplit;
+            for (int it = G - 1 - c; it < ap.items; it += G) {
+                const int per_head = ap.hsplit * ap.rsplit, rem = it % per_head, h = it / per_head;
+                const int ci = rem / ap.rsplit, rh = rem % ap.rsplit;
+                const int j0 = ci * (bph / ap.hsplit), j1 = j0 + bph / ap.hsplit;
+                int rt0, rt1;  // this item's row tiles of its wo columns
+                AttnRows(ntiles_dim, ap.rsplit, rh, rt0, rt1);
+                const int r0 = rt0 * 16, nrows = (rt1 * 16 < p.dim ? rt1 * 16 : p.dim) - r0;
                 const int hd = p.hd, half = hd / 2, kvh = h / p.group;
                 const size_t pstride = size_t(p.n_kv) * hd;
                 const size_t lbase = size_t(l) * p.max_seq * pstride + size_t(kvh) * hd;
@@ -812,7 +841,7 @@ __device__ unsigned Consumers(const MegaParams& p, const MkSmem& s) {
                     kn[b2] = __fadd_rn(__fmul_rn(x0, sn), __fmul_rn(x1, cs));
                 }
                 ConsumerBar();
-                if (h % p.group == 0 && j0 == 0)  // one CTA of the group's first head stores k, v
+                if (h % p.group == 0 && j0 == 0 && rh == 0)  // one CTA of the group's first head stores k, v
                     for (int i = tid; i < hd; i += 256) {
                         p.kc[lbase + size_t(pos) * pstride + i] = kn[i];
                         p.vc[lbase + size_t(pos) * pstride + i] = vn[i];
@@ -955,12 +984,12 @@ __device__ unsigned Consumers(const MegaParams& p, const MkSmem& s) {
                 // this item's wo block columns into acc, then one red.add pass
                 for (int j = j0; j < j1; ++j) {
                     WaitChunk(p, s, rg);
-                    ColumnDotSmem(L, StagePtr(p, s, rg), ntiles_dim, p.dim,
-                                  s.vdig + j * 32, vstride, s.vsx + j, s.acc);
+                    ColumnDotSmem(L, StagePtr(p, s, rg), rt1 - rt0, nrows, s.vdig + j * 32, vstride, s.vsx + j,
+                                  s.acc + r0);
                     ReleaseChunk(p, s, rg);
                 }
                 if (!WaitCounter(p, s, kMkPhases * l + 0, k1)) return rg.n;  // x_mid holds x
-                FlushRed(s.acc, p.xmid, p.dim, nullptr);
+                FlushRed(s.acc + r0, p.xmid + r0, nrows, nullptr);
                 Trace(p, step, l, 9);
                 Signal(p, kMkPhases * l + 1);
                 Trace(p, step, l, 3);
@@ -1154,8 +1183,8 @@ int MegaListCap(const MegaParams& p, int G) {
     auto per = [G](int items) { return (items + G - 1) / G; };  // items of one CTA at most
     const int t_qkv = (p.qd + 15) / 16 + 2 * ((p.kd + 15) / 16);
     const int t_lm = (p.vocab + 15) / 16;
-    const int hsplit = HeadSplit(p, G);
-    return p.n_layers * (per(t_qkv) + per(p.n_heads * hsplit) * (p.hd / 32 / hsplit) + 3 * per(p.hidden / 32)) +
+    const AttnPlan ap = AttnSplit(p, G);
+    return p.n_layers * (per(t_qkv) + per(ap.items) * (p.hd / 32 / ap.hsplit) + 3 * per(p.hidden / 32)) +
            per((t_lm + 1) / 2);
 }
 
