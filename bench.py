@@ -209,6 +209,7 @@ def run_ours(args):
     import torch
 
     from mini_llama_b200 import capi
+    from mini_llama_b200 import synth
     from mini_llama_b200.device import DeviceArray, Model, Session
 
     world = int(os.environ.get("WORLD_SIZE", "1"))
@@ -236,8 +237,7 @@ def run_ours(args):
     if args.graph:
         sess.use_persistent(False)
     path = sess.path()
-    from oracle.binding import Oracle  # only for the prompt ids (seeded generator)
-    prompt = Oracle().tokens(PROMPT, QWEN2["prompt_seed"], QWEN2["vocab_size"])
+    prompt = synth.tokens(PROMPT, QWEN2["prompt_seed"], QWEN2["vocab_size"])
     if args.no_prefill:  # profiling runs: decode from position 64 over an empty cache
         first = np.array([int(prompt[-1])], np.int32)
     else:

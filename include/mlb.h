@@ -306,6 +306,14 @@ int mlb_session_use_persistent(mlb_session* session, int enable);
 int mlb_session_trace(mlb_session* session, unsigned long long* device_buffer, size_t entries);
 /* Device pointers of the session KV cache. */
 int mlb_session_kv_cache(mlb_session* session, float** key_cache, float** value_cache);
+/* Prompts of at least min_tokens tokens (default 16; 0: never) go through
+ * mlb_session_generate in one pass -- every layer on all prompt tokens at
+ * once, each linear one call on n_prompt rows (tcgen05 tensor cores from 9),
+ * RoPE and the KV write for all positions, then causal attention as a batch
+ * of queries over the cache -- instead of one decode step per token.  The
+ * per-position computation is the same; the reference processes prompts one
+ * token at a time (ForwardBatch, src/forward.cpp:668-684). */
+int mlb_session_prefill_min(mlb_session* session, int min_tokens);
 
 /* ------------------------------------------------------------ batched decode
  * A batch of independent sequences decoded in lockstep through one model:

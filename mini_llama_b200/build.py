@@ -68,8 +68,7 @@ def build(verbose: bool = False, force: bool = False) -> str:
     with concurrent.futures.ThreadPoolExecutor(max_workers=os.cpu_count() or 4) as ex:
         list(ex.map(run, jobs))
     if jobs or not os.path.exists(LIB):
-        run([nvcc(), "-shared", "-gencode", "arch=compute_100a,code=sm_100a", "-o", LIB, *objs,
-             "-lcuda"])
+        run([nvcc(), "-shared", "-gencode", "arch=compute_100a,code=sm_100a", "-o", LIB, *objs])
     return LIB
 
 

@@ -103,6 +103,7 @@ SIGNATURES = {
     "mlb_session_use_persistent": (_i, [_vp, _i]),
     "mlb_session_trace": (_i, [_vp, _vp, _sz]),
     "mlb_session_kv_cache": (_i, [_vp, _pp, _pp]),
+    "mlb_session_prefill_min": (_i, [_vp, _i]),
     "mlb_nccl_unique_id": (_i, [_vp]),
     "mlb_batch_shard": (_i, [ctypes.POINTER(ModelConfig), _i, _i, _pi]),
     "mlb_batch_create": (_i, [_vp, _i, _i, _i, _vp, _pp]),

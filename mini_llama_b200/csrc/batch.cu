@@ -35,6 +35,7 @@
 #include "attention.cuh"
 #include "model.cuh"
 #include "qgemv.cuh"
+#include "rows.cuh"
 
 struct mlb_batch {
     mlb_model* model = nullptr;
@@ -111,17 +112,6 @@ void CheckNccl(ncclResult_t r, const char* what) {
         Fail(MLB_ERR_CUDA, std::string(what) + ": " + Nccl().error_string(r));
 }
 
-__device__ __forceinline__ float BlockSumRow(float v, float* scratch) {
-    v = WarpSum(v);
-    const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
-    if (lane == 0) scratch[warp] = v;
-    __syncthreads();
-    float t = 0.0f;
-    for (int w = 0; w < (blockDim.x >> 5); ++w) t += scratch[w];
-    __syncthreads();
-    return t;
-}
-
 // x[b] = table[hist[b][pos]]; an out-of-range token records the status and
 // leaves zeros.
 __global__ void BatchEmbedKernel(const float* table, int vocab, int dim, const int* hist, int hist_stride,
@@ -136,21 +126,6 @@ __global__ void BatchEmbedKernel(const float* table, int vocab, int dim, const i
     for (int i = threadIdx.x; i < dim; i += blockDim.x) x[size_t(b) * dim + i] = ok ? row[i] : 0.0f;
 }
 
-// y[b] = x[b] * rsqrt(mean(x[b]^2) + eps) * w, one CTA per row (the order of
-// the final products of src/ops.cpp:49-69).
-__global__ void BatchRmsNormKernel(const float* x, const float* w, float* y, int n, float eps) {
-    __shared__ float scratch[32];
-    GridDepWait();
-    GridDepLaunch();
-    const float* xr = x + size_t(blockIdx.x) * n;
-    float* yr = y + size_t(blockIdx.x) * n;
-    float ss = 0.0f;
-    for (int i = threadIdx.x; i < n; i += blockDim.x) ss = fmaf(xr[i], xr[i], ss);
-    ss = BlockSumRow(ss, scratch);
-    const float scale = 1.0f / sqrtf(ss / static_cast<float>(n) + eps);
-    for (int i = threadIdx.x; i < n; i += blockDim.x) yr[i] = xr[i] * scale * w[i];
-}
-
 // dst[b][r * n + j] = src[r][b][j] (+ add[b][r * n + j]): all-gathered slices
 // back into rows.
 __global__ void GatherKernel(const float* src, int ranks, int batch, int n, const float* add, float* dst) {
@@ -162,16 +137,6 @@ __global__ void GatherKernel(const float* src, int ranks, int batch, int n, cons
         const size_t r = c / n, j = c - r * n;
         const float v = src[(r * batch + b) * n + j];
         dst[i] = add ? add[i] + v : v;
-    }
-}
-
-// y = silu(g) * u (SiLU of src/ops.cpp: x / (1 + e^-x)).
-__global__ void SwigluKernel(const float* g, const float* u, size_t n, float* y) {
-    GridDepWait();
-    GridDepLaunch();
-    for (size_t i = blockIdx.x * size_t(blockDim.x) + threadIdx.x; i < n; i += size_t(gridDim.x) * blockDim.x) {
-        const float a = g[i];
-        y[i] = a / (1.0f + expf(-a)) * u[i];
     }
 }
 
@@ -304,7 +269,7 @@ void CaptureBatchStep(mlb_batch* s, DeviceContext& c) {
                const_cast<const int*>(s->hist), hist_stride, const_cast<const int*>(s->state), s->x, status);
         for (int l = 0; l < cf.n_layers; ++l) {
             // 1. RMSNorm, this rank's q / k / v rows (+ bias)
-            Launch("BatchRmsNormKernel", BatchRmsNormKernel, dim3(B), dim3(kRowThreads), 0, st, true,
+            Launch("RowsRmsNormKernel", RowsRmsNormKernel, dim3(B), dim3(kRowThreads), 0, st, true,
                    const_cast<const float*>(s->x), F(l, MLB_W_ATTN_NORM), s->xn, cf.dim, cf.rms_norm_eps);
             const float* bq = cf.qkv_bias ? F(l, MLB_W_BQ) + size_t(s->h0) * hd : nullptr;
             const float* bk = cf.qkv_bias ? F(l, MLB_W_BK) + size_t(s->k0) * hd : nullptr;
@@ -352,11 +317,11 @@ void CaptureBatchStep(mlb_batch* s, DeviceContext& c) {
             linear(s->attn, Rows(m, l, MLB_W_WO, s->d0, qd), qd, dl, nullptr, s->o_l);
             gather(s->o_l, dl, s->x, s->xmid);
             // 4. RMSNorm, this rank's gate / up rows, SwiGLU
-            Launch("BatchRmsNormKernel", BatchRmsNormKernel, dim3(B), dim3(kRowThreads), 0, st, true,
+            Launch("RowsRmsNormKernel", RowsRmsNormKernel, dim3(B), dim3(kRowThreads), 0, st, true,
                    const_cast<const float*>(s->xmid), F(l, MLB_W_FFN_NORM), s->xn, cf.dim, cf.rms_norm_eps);
             linear(s->xn, Rows(m, l, MLB_W_GATE, s->f0, cf.dim), cf.dim, fl, nullptr, s->gate);
             linear(s->xn, Rows(m, l, MLB_W_UP, s->f0, cf.dim), cf.dim, fl, nullptr, s->up);
-            Launch("SwigluKernel", SwigluKernel, dim3(GridFor(size_t(B) * fl, 256, c.sm_count)), dim3(256), 0, st,
+            Launch("RowsSwigluKernel", RowsSwigluKernel, dim3(GridFor(size_t(B) * fl, 256, c.sm_count)), dim3(256), 0, st,
                    true, const_cast<const float*>(s->gate), const_cast<const float*>(s->up), size_t(B) * fl,
                    s->sw_l);
             // 5. whole SwiGLU rows -> this rank's down rows -> x = x_mid + all rows
@@ -365,7 +330,7 @@ void CaptureBatchStep(mlb_batch* s, DeviceContext& c) {
             gather(s->d_l, dl, s->xmid, s->x);
         }
         // final RMSNorm, this rank's vocabulary rows, arg-max merged over ranks
-        Launch("BatchRmsNormKernel", BatchRmsNormKernel, dim3(B), dim3(kRowThreads), 0, st, true,
+        Launch("RowsRmsNormKernel", RowsRmsNormKernel, dim3(B), dim3(kRowThreads), 0, st, true,
                const_cast<const float*>(s->x), static_cast<const float*>(m->Ptr(m->global[MLB_W_FINAL_NORM])), s->xn,
                cf.dim, cf.rms_norm_eps);
         linear(s->xn, Rows(m, -1, MLB_W_LM_HEAD, s->v0, cf.dim), cf.dim, vl, nullptr, s->logits);

@@ -29,6 +29,7 @@
 #include "model.cuh"
 #include "qgemv.cuh"
 #include "qmma.cuh"
+#include "rows.cuh"
 
 namespace mlb {
 
@@ -92,6 +93,14 @@ struct mlb_session {
     unsigned tag_base = 1;               // next (step 0, layer 0) tag; 0 marks never written
     cudaGraph_t graph = nullptr;
     cudaGraphExec_t exec = nullptr;
+    // prompt pass: all prompt tokens through each layer at once (row buffers
+    // for max_seq_len tokens, allocated on first use)
+    int prefill_min = 16;  // prompts of at least this many tokens take it (0: never)
+    bool pf_ready = false;
+    float *pf_x = nullptr, *pf_xn = nullptr, *pf_q = nullptr, *pf_k = nullptr, *pf_v = nullptr;
+    float *pf_attn = nullptr, *pf_o = nullptr, *pf_xmid = nullptr, *pf_gate = nullptr, *pf_up = nullptr;
+    float *pf_sw = nullptr, *pf_d = nullptr, *pf_part_ml = nullptr, *pf_part_o = nullptr;
+    int* pf_pos = nullptr;
     std::vector<void*> allocations;
 };
 
@@ -511,11 +520,162 @@ void RunMega(mlb_session* s, DeviceContext& c, int start_pos, int n_steps, int g
     LaunchMegaDecode(p, c.sm_count, s->mega_smem, c.stream);
 }
 
+// First maximum of x[0..n) (src/ops.cpp:199-212) into hist[slot] (when slot
+// >= 0) and *token; one CTA.
+__global__ void PrefillArgmaxKernel(const float* x, int n, int* hist, int slot, int* token) {
+    __shared__ float sv[1024];
+    __shared__ int si[1024];
+    GridDepWait();
+    GridDepLaunch();
+    float bv = -INFINITY;
+    int bi = 0x7fffffff;
+    for (int i = threadIdx.x; i < n; i += blockDim.x)
+        if (x[i] > bv || (x[i] == bv && i < bi)) {
+            bv = x[i];
+            bi = i;
+        }
+    sv[threadIdx.x] = bv;
+    si[threadIdx.x] = bi;
+    __syncthreads();
+    for (int o = blockDim.x / 2; o > 0; o >>= 1) {
+        if (threadIdx.x < o) {
+            const float ov = sv[threadIdx.x + o];
+            const int oi = si[threadIdx.x + o];
+            if (ov > sv[threadIdx.x] || (ov == sv[threadIdx.x] && oi < si[threadIdx.x])) {
+                sv[threadIdx.x] = ov;
+                si[threadIdx.x] = oi;
+            }
+        }
+        __syncthreads();
+    }
+    if (threadIdx.x == 0) {
+        const int tok = si[0] == 0x7fffffff ? 0 : si[0];
+        *token = tok;
+        if (slot >= 0) hist[slot] = tok;
+    }
+}
+
+void EnsurePrefill(mlb_session* s, DeviceContext& c) {
+    if (s->pf_ready) return;
+    const mlb_model_config& cf = s->model->cfg;
+    const size_t R = size_t(cf.max_seq_len);
+    const int qd = cf.n_heads * cf.head_dim, kd = cf.n_kv_heads * cf.head_dim;
+    auto A = [&](size_t floats) { return static_cast<float*>(DevAlloc(s, c, std::max<size_t>(floats, 1) * 4)); };
+    s->pf_x = A(R * cf.dim);
+    s->pf_xn = A(R * cf.dim);
+    s->pf_xmid = A(R * cf.dim);
+    s->pf_o = A(R * cf.dim);
+    s->pf_d = A(R * cf.dim);
+    s->pf_q = A(R * qd);
+    s->pf_attn = A(R * qd);
+    s->pf_k = A(R * kd);
+    s->pf_v = A(R * kd);
+    s->pf_gate = A(R * cf.hidden_dim);
+    s->pf_up = A(R * cf.hidden_dim);
+    s->pf_sw = A(R * cf.hidden_dim);
+    s->pf_part_ml = A(R * cf.n_heads * s->chunks * 2);
+    s->pf_part_o = A(R * cf.n_heads * s->chunks * cf.head_dim);
+    s->pf_pos = static_cast<int*>(DevAlloc(s, c, R * 4));
+    s->pf_ready = true;
+}
+
+// Tokens hist[start .. start + n) through every layer at once: each linear is
+// one call on n rows (the tcgen05 path from 9 rows), RoPE and the KV write
+// for all n positions first, then causal attention as a batch of n queries
+// over the session's cache (query i sees positions 0 .. start + i).  The last
+// row's logits land in s->logits and their first arg-max in hist[start + n]
+// (and state[2]).  The work per sequence position is the decode step's.
+void Prefill(mlb_session* s, DeviceContext& c, int start, int n) {
+    mlb_model* m = s->model;
+    const mlb_model_config& cf = m->cfg;
+    const int qt = cf.weight_type, hd = cf.head_dim, D = cf.dim, F = cf.hidden_dim;
+    const int qd = cf.n_heads * hd, kd = cf.n_kv_heads * hd;
+    cudaStream_t st = c.stream;
+    int* status = s->state + 3;
+    auto W = [&](int l, int kind) { return static_cast<const uint8_t*>(m->Ptr(m->Get(l, kind))); };
+    auto Fv = [&](int l, int kind) { return static_cast<const float*>(m->Ptr(m->Get(l, kind))); };
+    // (not captured into a graph: the tensor-core linears use the context's workspace)
+    auto linear = [&](const float* x, const uint8_t* w, int rows, int K, int N, const float* bias, float* y) {
+        LinearRows(c, qt, x, w, rows, K, N, bias, y);
+    };
+    auto rms = [&](const float* x, const float* w, float* y, int rows) {
+        Launch("RowsRmsNormKernel", RowsRmsNormKernel, dim3(rows), dim3(256), 0, st, true, x, w, y, D,
+               cf.rms_norm_eps);
+    };
+    auto add = [&](const float* a, const float* b, float* y, size_t cnt) {
+        Launch("RowsAddKernel", RowsAddKernel, dim3(RowsGrid(cnt, 256, c.sm_count)), dim3(256), 0, st, true, a, b,
+               cnt, y);
+    };
+    const int hgroups = (cf.n_heads / cf.n_kv_heads + kAttnGmax - 1) / kAttnGmax;
+    const int chunks = std::min(s->chunks, AttnChunks(start + n, n, cf.n_kv_heads, hgroups, c.sm_count));
+    Launch("RowsEmbedKernel", RowsEmbedKernel, dim3(n), dim3(256), 0, st, true,
+           static_cast<const float*>(m->Ptr(m->global[MLB_W_EMBEDDING])), cf.vocab_size, D,
+           const_cast<const int*>(s->hist + start), s->pf_x, status);
+    for (int l = 0; l < cf.n_layers; ++l) {
+        rms(s->pf_x, Fv(l, MLB_W_ATTN_NORM), s->pf_xn, n);
+        linear(s->pf_xn, W(l, MLB_W_WQ), n, D, qd, cf.qkv_bias ? Fv(l, MLB_W_BQ) : nullptr, s->pf_q);
+        linear(s->pf_xn, W(l, MLB_W_WK), n, D, kd, cf.qkv_bias ? Fv(l, MLB_W_BK) : nullptr, s->pf_k);
+        linear(s->pf_xn, W(l, MLB_W_WV), n, D, kd, cf.qkv_bias ? Fv(l, MLB_W_BV) : nullptr, s->pf_v);
+        Launch("RowsRopeKvKernel", RowsRopeKvKernel, dim3(n), dim3(256), 0, st, true, s->pf_q,
+               const_cast<const float*>(s->pf_k), const_cast<const float*>(s->pf_v), cf.n_heads, cf.n_kv_heads, hd,
+               start, const_cast<const float*>(m->rope_cos), const_cast<const float*>(m->rope_sin),
+               cf.rope_type == MLB_ROPE_NEOX ? 1 : 0, s->kc, s->vc, l, cf.max_seq_len, s->pf_pos);
+        AttnParams a = {};
+        a.q = s->pf_q;
+        a.q_batch_stride = size_t(qd);
+        a.kc = s->kc;
+        a.vc = s->vc;
+        a.seq_stride = 0;  // every query reads the session's one cache
+        a.layer = l;
+        a.max_seq_len = cf.max_seq_len;
+        a.n_heads = cf.n_heads;
+        a.n_kv = cf.n_kv_heads;
+        a.hd = hd;
+        a.group = cf.n_heads / cf.n_kv_heads;
+        a.hgroups = hgroups;
+        a.chunks = chunks;
+        a.scale = 1.0f / std::sqrt(static_cast<float>(hd));
+        a.pos_dev = s->pf_pos;
+        a.pos_stride = 1;
+        a.out = s->pf_attn;
+        a.part_ml = s->pf_part_ml;
+        a.part_o = s->pf_part_o;
+        a.fused_rope = 0;
+        LaunchAttention(a, n, st, true);
+        if (chunks > 1) {
+            AttnMergeKernel<<<n * cf.n_heads, 128, 0, st>>>(s->pf_part_ml, s->pf_part_o, chunks, hd, s->pf_attn);
+            CheckCuda(cudaGetLastError(), "AttnMergeKernel");
+        }
+        linear(s->pf_attn, W(l, MLB_W_WO), n, qd, D, nullptr, s->pf_o);
+        add(s->pf_x, s->pf_o, s->pf_xmid, size_t(n) * D);
+        rms(s->pf_xmid, Fv(l, MLB_W_FFN_NORM), s->pf_xn, n);
+        linear(s->pf_xn, W(l, MLB_W_GATE), n, D, F, nullptr, s->pf_gate);
+        linear(s->pf_xn, W(l, MLB_W_UP), n, D, F, nullptr, s->pf_up);
+        Launch("RowsSwigluKernel", RowsSwigluKernel, dim3(RowsGrid(size_t(n) * F, 256, c.sm_count)), dim3(256), 0,
+               st, true, const_cast<const float*>(s->pf_gate), const_cast<const float*>(s->pf_up), size_t(n) * F,
+               s->pf_sw);
+        linear(s->pf_sw, W(l, MLB_W_DOWN), n, F, D, nullptr, s->pf_d);
+        add(s->pf_xmid, s->pf_d, s->pf_x, size_t(n) * D);
+    }
+    // the last token: final RMSNorm, lm_head, arg-max
+    rms(s->pf_x + size_t(n - 1) * D, static_cast<const float*>(m->Ptr(m->global[MLB_W_FINAL_NORM])), s->pf_xn, 1);
+    linear(s->pf_xn, W(-1, MLB_W_LM_HEAD), 1, D, cf.vocab_size, nullptr, s->logits);
+    Launch("PrefillArgmaxKernel", PrefillArgmaxKernel, dim3(1), dim3(1024), 0, st, true,
+           const_cast<const float*>(s->logits), cf.vocab_size, s->hist, start + n <= cf.max_seq_len ? start + n : -1,
+           s->state + 2);
+}
+
 void CheckStatus(mlb_session* s, DeviceContext& c) {
     int status = 0;
     CheckCuda(cudaMemcpyAsync(&status, s->state + 3, sizeof(int), cudaMemcpyDeviceToHost, c.stream),
               "cudaMemcpyAsync(status)");
     CheckCuda(cudaStreamSynchronize(c.stream), "cudaStreamSynchronize");
+    if (status == 0) {  // the tensor-core linears of the prompt pass report into the context's word
+        CheckCuda(cudaMemcpyAsync(&status, c.status, sizeof(int), cudaMemcpyDeviceToHost, c.stream),
+                  "cudaMemcpyAsync(status)");
+        CheckCuda(cudaStreamSynchronize(c.stream), "cudaStreamSynchronize");
+        if (status != 0) CheckCuda(cudaMemsetAsync(c.status, 0, sizeof(int), c.stream), "cudaMemsetAsync");
+    }
     if (status != 0) {
         CheckCuda(cudaMemsetAsync(s->state + 3, 0, sizeof(int), c.stream), "cudaMemsetAsync");
         Fail(status, status == MLB_ERR_DEVICE_TIMEOUT
@@ -755,13 +915,29 @@ int mlb_session_generate(mlb_session* session, const int* prompt, int n_prompt, 
         CheckCuda(cudaMemcpyAsync(session->hist + start_pos, prompt, size_t(n_prompt) * 4,
                                   cudaMemcpyHostToDevice, c.stream),
                   "cudaMemcpyAsync(prompt)");
-        SetState(session, c, start_pos, start_pos + n_prompt);
-        const int steps = n_prompt + n_new - 1;
-        if (session->mega) {
-            RunMega(session, c, start_pos, steps, start_pos + n_prompt);
+        if (session->prefill_min > 0 && n_prompt >= session->prefill_min) {
+            // the prompt in one pass, then the remaining n_new - 1 decode steps
+            EnsurePrefill(session, c);
+            Prefill(session, c, start_pos, n_prompt);
+            const int from = start_pos + n_prompt;
+            if (n_new > 1) {
+                SetState(session, c, from, from);
+                if (session->mega) {
+                    RunMega(session, c, from, n_new - 1, from);
+                } else {
+                    for (int i = 0; i < n_new - 1; ++i)
+                        CheckCuda(cudaGraphLaunch(session->exec, c.stream), "cudaGraphLaunch");
+                }
+            }
         } else {
-            for (int i = 0; i < steps; ++i)
-                CheckCuda(cudaGraphLaunch(session->exec, c.stream), "cudaGraphLaunch");
+            SetState(session, c, start_pos, start_pos + n_prompt);
+            const int steps = n_prompt + n_new - 1;
+            if (session->mega) {
+                RunMega(session, c, start_pos, steps, start_pos + n_prompt);
+            } else {
+                for (int i = 0; i < steps; ++i)
+                    CheckCuda(cudaGraphLaunch(session->exec, c.stream), "cudaGraphLaunch");
+            }
         }
         CheckCuda(cudaMemcpyAsync(out_tokens, session->hist + start_pos + n_prompt, size_t(n_new) * 4,
                                   cudaMemcpyDeviceToHost, c.stream),
@@ -827,6 +1003,14 @@ int mlb_session_use_persistent(mlb_session* session, int enable) {
         DeviceContext& c = Ctx(session->model->device);
         CheckCuda(cudaStreamSynchronize(c.stream), "cudaStreamSynchronize");
         session->mega = enable != 0;
+    });
+}
+
+int mlb_session_prefill_min(mlb_session* session, int min_tokens) {
+    return Guard([&] {
+        Require(session != nullptr, "mlb_session_prefill_min", "null argument");
+        Require(min_tokens >= 0, "mlb_session_prefill_min", "min_tokens must not be negative");
+        session->prefill_min = min_tokens;
     });
 }
 

@@ -184,6 +184,10 @@ class Session:
     def use_persistent(self, enable: bool):
         self.lib.call("mlb_session_use_persistent", self.handle, 1 if enable else 0)
 
+    def prefill_min(self, min_tokens: int):
+        """Prompts of at least min_tokens tokens take the one-pass prompt path (0: never)."""
+        self.lib.call("mlb_session_prefill_min", self.handle, int(min_tokens))
+
     def logits_ptr(self) -> int:
         p = ctypes.c_void_p()
         self.lib.call("mlb_session_logits", self.handle, ctypes.byref(p))

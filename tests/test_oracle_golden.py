@@ -8,7 +8,7 @@ here is bit equality, not a tolerance.
 import numpy as np
 import pytest
 
-from oracle.binding import Q40, Q41, Q80, STREAM_W, STREAM_X
+from oracle.binding import Q40, Q41, Q80, STREAM_W, STREAM_X, Oracle
 
 LINEAR_SHAPES = [(5, 13), (5, 32), (5, 33), (5, 64), (5, 129), (7, 176), (16, 896), (3, 4864)]
 
@@ -202,3 +202,11 @@ def test_model_qwen2_prefix(oracle, golden_qwen2):
     # 64 prompt positions plus the first 3 greedy steps; the complete 191-step
     # run is exercised by the GPU parity tests against the same fixture.
     check_model(oracle, golden_qwen2, "qwen2", 64, 128, False, max_steps=67)
+
+
+def test_bench_prompt_ids_match_oracle_generator():
+    """bench.py draws its prompt ids with the package's host generator; they
+    are the oracle's seeded prompt stream."""
+    from mini_llama_b200 import synth
+    for n, seed, vocab in ((64, 3, 151936), (17, 1, 32000), (5, 42, 256)):
+        assert np.array_equal(synth.tokens(n, seed, vocab), np.asarray(Oracle().tokens(n, seed, vocab)))
