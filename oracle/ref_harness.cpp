@@ -8,6 +8,9 @@
 //                                            time the reference RunBenchmark
 //                                            (src/debug.cpp:79-143); one JSON
 //                                            line per step on stdout
+//   ref_harness gguf <file> <prompt_len> <n_new> <seed>
+//                                            load a GGUF file (LoadGgufModel)
+//                                            and decode greedily; one JSON line
 //
 // Every numeric result comes from the reference's own functions: QuantizeToQ80/
 // Q40 and DeQuantize* (src/quant.cpp), LinearQ80/Q40/Q41 (src/quant.cpp:409-418),
@@ -36,6 +39,7 @@
 #include "include/ops.h"
 #include "include/quant.h"
 #include "include/thread_pool.h"
+#include "ref_gguf_run.h"
 #include "ref_models.h"
 #include "synth.h"
 
@@ -334,6 +338,17 @@ int main(int argc, char** argv) {
             if (on("tiny")) CaseModel("tiny", 4, 8, true);
             if (on("llama2_l2")) CaseModel("llama2_l2", 6, 6, false);
             if (on("qwen2")) CaseModel("qwen2", 64, 128, false);
+            return 0;
+        }
+        if (argc == 6 && std::string(argv[1]) == "gguf") {
+            MiniLlamaModel model = LoadGgufOrThrow(argv[2]);
+            const GgufRun r = RunGguf(model, GgufPrompt(model, std::atoi(argv[3]), std::strtoull(argv[5], nullptr, 10)),
+                                      std::atoi(argv[4]));
+            std::printf("{\"tokens\": [");
+            for (size_t i = 0; i < r.tokens.size(); ++i) std::printf("%s%d", i ? ", " : "", r.tokens[i]);
+            std::printf("], \"neox\": %d, \"vocab\": %d, \"dim\": %d, \"head_dim\": %d, \"lm_head_f32\": %d}\n",
+                        model.config.rope_type == RopeType::kNeoX ? 1 : 0, model.config.vocab_size,
+                        model.config.dim, model.config.head_dim, model.lm_head.type == QuantType::kF32 ? 1 : 0);
             return 0;
         }
         if (argc == 8 && std::string(argv[1]) == "bench") {
