@@ -496,6 +496,15 @@ void PrepareMega(mlb_session* s, DeviceContext& c) {
     p.status = s->state + 3;
     p.stage_bytes = stage_bytes;
     p.list_cap = MegaListCap(p, c.sm_count);
+    // cached K rows of the first attention pass in shared memory, as many as
+    // the limit leaves room for (a multiple of 8, at most one pass)
+    p.kst_rows = 0;
+    const size_t smem0 = MegaSmemBytes(p), optin = static_cast<size_t>(c.max_smem_optin);
+    if (smem0 < optin) {
+        size_t rows = (optin - smem0) / (4 * size_t(p.hd));
+        rows = std::min<size_t>({rows, size_t(kMkAttnChunk), size_t(p.max_seq)});
+        p.kst_rows = static_cast<int>(rows & ~size_t(7));
+    }
     s->mega_smem = MegaSmemBytes(p);
     s->mega_reason = MegaFits(p, s->mega_smem, c.sm_count);
     s->mega_ok = s->mega_reason.empty();

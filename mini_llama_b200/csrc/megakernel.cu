@@ -38,6 +38,16 @@ __device__ __forceinline__ unsigned long long LdTagged(const unsigned long long*
     return w;
 }
 
+// A 16-byte L2 load as a volatile asm statement: it keeps its place among the
+// other volatile statements (issued before a polling loop, not sunk past it).
+__device__ __forceinline__ float4 LdCgF4(const float* p) {
+    float4 v;
+    asm volatile("ld.global.cg.v4.f32 {%0, %1, %2, %3}, [%4];"
+                 : "=f"(v.x), "=f"(v.y), "=f"(v.z), "=f"(v.w)
+                 : "l"(p));
+    return v;
+}
+
 __device__ __forceinline__ void RedAdd(float* p, float v) {
     asm volatile("red.global.add.f32 [%0], %1;" ::"l"(p), "f"(v) : "memory");
 }
@@ -85,6 +95,7 @@ struct MkSmem {  // flags[0] is the CTA's abort flag (read by the producer warp 
     float* att;     // [8 warps][hd] attention partials
     float* sc;      // [kMkAttnChunk] scores / weights of a chunk of positions
     float* acc;     // [dim] block-column products of the CTA, flushed by red.add
+    float* kst;     // [kst_rows][hd] cached K rows of the attention item's KV head (swizzled)
     float* scratch; // [32]
     int* flags;     // [0] abort, [1] token, [2] chunks per step, [4] decision, [5] chunks issued
 };
@@ -773,21 +784,28 @@ __device__ unsigned Consumers(const MegaParams& p, const MkSmem& s) {
                 const size_t lbase = size_t(l) * p.max_seq * pstride + size_t(kvh) * hd;
                 const int lpr = hd / 4, rpi = 32 / lpr;  // float4 lanes per K/V row, rows per warp pass
                 const int rsub = lane / lpr, col = lane % lpr;
-                // While QKV runs: the K row of cached position tid (first
-                // chunk; its first 64 floats) into registers, every cached V
-                // row and the K rows of later chunks into L2.  None depend on
-                // this step.
-                float4 kpre[16];
-                {
-                    const bool kp = tid < pos;
-                    const float4* kr = reinterpret_cast<const float4*>(p.kc + lbase + size_t(kp ? tid : 0) * pstride);
+                // While QKV runs (none of it depends on the step): the K rows
+                // of cached positions 0..nst-1 into shared memory (cp.async;
+                // 16-byte piece c of row r at slot c ^ (r % 8), so the score
+                // pass reads a row per thread without bank conflicts), this
+                // warp's V row pieces of the first pass into registers (the
+                // asm loads keep their place before the q, k, v polls), the
+                // other cached rows into L2.
+                const int nst = pos < p.kst_rows ? pos : p.kst_rows;
+                for (int i = tid; i < nst * lpr; i += 256) {
+                    const int r = i / lpr, c4 = i - r * lpr;
+                    CpAsync16(s.kst + r * hd + 4 * (c4 ^ (r & 7)), p.kc + lbase + size_t(r) * pstride + 4 * c4);
+                }
+                float4 vpre[16];
 #pragma unroll
-                    for (int i = 0; i < 16; ++i)
-                        kpre[i] = kp && i < lpr ? __ldcg(kr + i) : make_float4(0.f, 0.f, 0.f, 0.f);
+                for (int i = 0; i < 16; ++i) {
+                    const int r = warp * 32 + i * rpi + rsub;
+                    vpre[i] = make_float4(0.f, 0.f, 0.f, 0.f);
+                    if (i < lpr && r < pos) vpre[i] = LdCgF4(p.vc + lbase + size_t(r) * pstride + 4 * col);
                 }
                 for (int pp = tid; pp < pos; pp += 256) {
                     BulkPrefetchL2(p.vc + lbase + size_t(pp) * pstride, static_cast<uint32_t>(hd) * 4);
-                    if (pp >= kMkAttnChunk)
+                    if (pp >= nst)
                         BulkPrefetchL2(p.kc + lbase + size_t(pp) * pstride, static_cast<uint32_t>(hd) * 4);
                 }
                 // RoPE rows of this position (s.att is free until the values pass)
@@ -822,7 +840,7 @@ __device__ unsigned Consumers(const MegaParams& p, const MkSmem& s) {
                     (part == 0 ? q : (part == 1 ? kn : vn))[d] = __uint_as_float(static_cast<unsigned>(wv));
                 }
                 for (int i = tid; i < hd; i += 256) o[i] = 0.0f;
-                CpAsyncWaitAll();  // this thread's RoPE-table copies; the barrier publishes them
+                CpAsyncWaitAll();  // this thread's RoPE-table and K-row copies; the barrier publishes them
                 ConsumerBar();
                 if (tid == 0) s.flags[4] = s.flags[0] == 0;
                 ConsumerBar();
@@ -867,23 +885,21 @@ __device__ unsigned Consumers(const MegaParams& p, const MkSmem& s) {
                                 dot = fmaf(qv.z, kv.z, dot);
                                 dot = fmaf(qv.w, kv.w, dot);
                             }
-                        } else {
-                            int i0 = 0;
-                            if (base == 0) {  // the prefetched part of the row, four chains
-                                float d4[4] = {0.f, 0.f, 0.f, 0.f};
+                        } else if (pp < nst) {  // a staged row (first pass), four chains
+                            const float4* ks = reinterpret_cast<const float4*>(s.kst + size_t(pp) * hd);
+                            float d4[4] = {0.f, 0.f, 0.f, 0.f};
 #pragma unroll
-                                for (int i = 0; i < 16; ++i)
-                                    if (i < lpr) {
-                                        const float4 qv = q4[i];
-                                        d4[i & 3] = fmaf(qv.x, kpre[i].x, d4[i & 3]);
-                                        d4[i & 3] = fmaf(qv.y, kpre[i].y, d4[i & 3]);
-                                        d4[i & 3] = fmaf(qv.z, kpre[i].z, d4[i & 3]);
-                                        d4[i & 3] = fmaf(qv.w, kpre[i].w, d4[i & 3]);
-                                    }
-                                dot = (d4[0] + d4[1]) + (d4[2] + d4[3]);
-                                i0 = 16;
-                            }
-                            for (; i0 < lpr; i0 += 8) {  // 8 loads in flight
+                            for (int i = 0; i < 32; ++i)
+                                if (i < lpr) {
+                                    const float4 qv = q4[i], kv = ks[i ^ (pp & 7)];
+                                    d4[i & 3] = fmaf(qv.x, kv.x, d4[i & 3]);
+                                    d4[i & 3] = fmaf(qv.y, kv.y, d4[i & 3]);
+                                    d4[i & 3] = fmaf(qv.z, kv.z, d4[i & 3]);
+                                    d4[i & 3] = fmaf(qv.w, kv.w, d4[i & 3]);
+                                }
+                            dot = (d4[0] + d4[1]) + (d4[2] + d4[3]);
+                        } else {
+                            for (int i0 = 0; i0 < lpr; i0 += 8) {  // 8 loads in flight
                                 float4 kv[8];
 #pragma unroll
                                 for (int i = 0; i < 8; ++i)
@@ -901,19 +917,21 @@ __device__ unsigned Consumers(const MegaParams& p, const MkSmem& s) {
                         }
                         sc = dot * p.scale;
                     }
-                    // this warp's first 16 V row pieces, loaded before the
-                    // softmax reductions so their latency overlaps them; the
-                    // current position's row comes from shared memory
+                    // this warp's first 16 V row pieces (the first pass's
+                    // were loaded before the wait; later passes load them
+                    // before the softmax reductions so their latency overlaps
+                    // them); the current position's row comes from shared memory
                     const int r0 = base + warp * 32;
-                    float4 vpre[16];
 #pragma unroll
                     for (int i = 0; i < 16; ++i) {
                         const int r = r0 + i * rpi + rsub;
-                        vpre[i] = make_float4(0.f, 0.f, 0.f, 0.f);
-                        if (i < lpr && r < pos)
-                            vpre[i] = __ldcg(reinterpret_cast<const float4*>(p.vc + lbase + size_t(r) * pstride) + col);
-                        else if (i < lpr && r == pos)
-                            vpre[i] = reinterpret_cast<const float4*>(vn)[col];
+                        if (base > 0) {
+                            vpre[i] = make_float4(0.f, 0.f, 0.f, 0.f);
+                            if (i < lpr && r < pos)
+                                vpre[i] =
+                                    __ldcg(reinterpret_cast<const float4*>(p.vc + lbase + size_t(r) * pstride) + col);
+                        }
+                        if (i < lpr && r == pos) vpre[i] = reinterpret_cast<const float4*>(vn)[col];
                     }
                     const float mc = ConsumerMax(sc, s.scratch);
                     const float mnew = fmaxf(m_run, mc);
@@ -1143,6 +1161,7 @@ __global__ void __launch_bounds__(kMkThreads, 1) MegaDecodeKernel(const MegaPara
     for (int i = threadIdx.x; i < p.dim; i += kMkThreads) s.acc[i] = 0.0f;
     s.list = reinterpret_cast<Chunk*>(smem + list_off);
     s.ring = smem + list_off + Round128(sizeof(Chunk) * size_t(p.list_cap));
+    s.kst = reinterpret_cast<float*>(s.ring + Round128(size_t(kMkStages) * p.stage_bytes));
     if (threadIdx.x == 0) {
         for (int i = 0; i < kMkStages; ++i) MbarInit(&s.full[i], 1);
         FenceMbarInit();
@@ -1192,7 +1211,7 @@ size_t MegaSmemBytes(const MegaParams& p) {
     const int nb_dim = p.dim / 32;
     return kOffFixedEnd + 3 * Round128(4 * size_t(p.dim)) + Round128(4 * size_t(DigitStride(nb_dim))) +
            Round128(4 * size_t(nb_dim)) + Round128(sizeof(Chunk) * size_t(p.list_cap)) +
-           size_t(kMkStages) * p.stage_bytes;
+           Round128(size_t(kMkStages) * p.stage_bytes) + 4 * size_t(p.hd) * p.kst_rows;
 }
 
 std::string MegaFits(const MegaParams& p, size_t smem, int sm_count) {

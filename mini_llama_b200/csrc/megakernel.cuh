@@ -87,6 +87,7 @@ struct MegaParams {
     int* status;
     int stage_bytes;
     int list_cap;  // capacity of the per-CTA chunk list (MegaListCap)
+    int kst_rows;  // cached K rows an attention item stages in shared memory (0..kMkAttnChunk)
     // optional timeline: [step][layer 0..n_layers][event][CTA] %globaltimer
     // stamps; null when off.  Events: QKV 0 wait done, 11 input normalised,
     // 10 products stored, 1 signalled; attention 2 wait done, 8 softmax.V

@@ -90,5 +90,6 @@ def test_gguf_model_decodes_on_this_library_as_on_the_reference_cpu(tmp_path, na
     scale = max(1.0, out["logit_scale"])
     assert out["linear_calls"] > 0, "the device path did not run"
     assert out["logit_err"] <= 1e-3 * scale, out
-    assert out["cpu_min_gap"] > 2e-3 * scale, f"near-tie in the reference logits: {out}"
+    # the reference's top-2 margin exceeds twice the difference, so no arg-max can flip
+    assert out["cpu_min_gap"] > 2 * out["logit_err"], f"near-tie in the reference logits: {out}"
     assert out["b200"] == out["cpu"], out
