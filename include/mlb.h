@@ -184,7 +184,7 @@ int mlb_attention_decode_batched(int device, int batch, const float* q, const fl
  * already holds all free device memory, or a thread that must not take the
  * allocator's locks or risk the device synchronisation that freeing memory
  * can cause.  No counterpart in the reference.
- * The split-K partials live in one fixed 16 MiB array inside the library
+ * The split-K partials live in one fixed 4 MiB array inside the library
  * image, present on every device that loads the library until the process
  * exits; a shape whose partials need more (n_heads x chunks x (head_dim + 2)
  * floats) is rejected with MLB_ERR_UNSUPPORTED.  The first call on a device

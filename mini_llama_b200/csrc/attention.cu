@@ -1,6 +1,9 @@
 // Decode-attention entry points (replace mini_llama include/cuda_attention.h:10-14).
+#include <cudaTypedefs.h>
+
 #include <algorithm>
 #include <cmath>
+#include <cstring>
 #include <mutex>
 #include <string>
 
@@ -9,39 +12,177 @@
 namespace mlb {
 
 int AttnChunks(int max_npos, int batch, int n_kv, int hgroups, int sm_count) {
-    // at most kAttnChunk positions per CTA (K and V of a chunk fit in shared
-    // memory); more chunks while the grid is below about two waves of SMs
-    (void)hgroups;
-    long long c = (max_npos + kAttnChunk - 1) / kAttnChunk;
-    long long base = 1LL * batch * n_kv;
+    const long long base = 1LL * batch * n_kv * std::max(1, hgroups);  // CTAs per chunk
+    const long long slots = 1LL * kAttnCtasPerSm * sm_count;            // resident CTAs
+    // short contexts: 64-position chunks, halved while the grid is below
+    // two waves of SMs (down to 16 positions)
+    long long c = (max_npos + 63) / 64;
     while (c * 2 * base <= 2LL * sm_count && c * 2 * 16 <= max_npos) c *= 2;
-    return static_cast<int>(std::max(1LL, c));
+    if (c * base <= slots) return static_cast<int>(std::max(1LL, c));
+    // long contexts: each CTA loops over the tiles of its chunk, so the grid
+    // needs only the resident CTAs; the first count from there whose waves are
+    // at least 95 % full (else the fullest one tried)
+    const long long c0 = std::max(1LL, slots / base);
+    long long best = c0;
+    double best_eff = 0.0;
+    for (long long k = c0; k <= std::min(c, 8 * c0); ++k) {
+        const long long ctas = k * base, waves = (ctas + slots - 1) / slots;
+        const double eff = static_cast<double>(ctas) / static_cast<double>(waves * slots);
+        if (eff > best_eff + 1e-9) {
+            best = k;
+            best_eff = eff;
+        }
+        if (eff >= 0.95) break;
+    }
+    return static_cast<int>(best);
 }
 
-template <int DPL>
-void LaunchAttnT(const AttnParams& p, int batch, cudaStream_t stream, bool pdl) {
-    const size_t smem = AttnSmemBytes(p.hd);
+namespace {
+
+// out[b][h][d] = sum_c e^(m_c - M) o_c[d] / sum_c e^(m_c - M) l_c, one CTA of
+// kAttnMergeThreads per (sequence, head): the chunk weights once into shared
+// memory (kAttnMergeBatch at a time), then (chunk slice, dimension) threads
+// over the unnormalised outputs, the slices summed at the end.
+constexpr int kAttnMergeThreads = 256;
+constexpr int kAttnMergeBatch = 1024;
+
+__global__ void __launch_bounds__(kAttnMergeThreads) AttnMergeKernel(const float* part_ml, const float* part_o,
+                                                                    int chunks, int hd, float* out) {
+    __shared__ float wt[kAttnMergeBatch];
+    __shared__ float sred[kAttnMergeThreads];
+    __shared__ float sden[kAttnWarps];
+    GridDepWait();
+    GridDepLaunch();
+    const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
+    const size_t bh = blockIdx.x;  // b * n_heads + h
+    const float* ml = part_ml + bh * chunks * 2;
+    const float* po = part_o + bh * chunks * hd;
+    float mx = -INFINITY;
+    for (int c = tid; c < chunks; c += kAttnMergeThreads) mx = fmaxf(mx, ml[2 * c]);
+    mx = WarpMax(mx);
+    if (lane == 0) sden[warp] = mx;
+    __syncthreads();
+    mx = sden[0];
+    for (int w = 1; w < kAttnWarps; ++w) mx = fmaxf(mx, sden[w]);
+    const int nsl = hd < kAttnMergeThreads ? kAttnMergeThreads / hd : 1;  // chunk slices
+    const int sl = tid / hd, d = tid - sl * hd;
+    float num = 0.0f, den = 0.0f;
+    for (int c0 = 0; c0 < chunks; c0 += kAttnMergeBatch) {
+        const int cn = min(kAttnMergeBatch, chunks - c0);
+        __syncthreads();  // wt of the previous batch (and sden) fully read
+        for (int c = tid; c < cn; c += kAttnMergeThreads) {
+            const float mc = ml[2 * (c0 + c)];
+            const float w = mc == -INFINITY ? 0.0f : expf(mc - mx);
+            wt[c] = w;
+            den = fmaf(w, ml[2 * (c0 + c) + 1], den);
+        }
+        __syncthreads();
+        if (sl < nsl)
+            for (int c = sl; c < cn; c += nsl) num = fmaf(wt[c], po[size_t(c0 + c) * hd + d], num);
+    }
+    den = WarpSum(den);
+    __syncthreads();
+    if (lane == 0) sden[warp] = den;
+    sred[tid] = num;
+    __syncthreads();
+    float tden = 0.0f;
+    for (int w = 0; w < kAttnWarps; ++w) tden += sden[w];
+    for (int dd = tid; dd < hd; dd += kAttnMergeThreads) {
+        float t = 0.0f;
+        for (int s = 0; s < nsl; ++s) t += sred[s * hd + dd];
+        out[bh * hd + dd] = tden > 0.0f ? t / tden : 0.0f;
+    }
+}
+
+// The driver's tensor-map encoder through the runtime (the library does not
+// link the driver library); null when the driver does not offer it.
+PFN_cuTensorMapEncodeTiled_v12000 TensorMapEncoder() {
+    static PFN_cuTensorMapEncodeTiled_v12000 encode = [] {
+        void* fn = nullptr;
+        cudaDriverEntryPointQueryResult q = cudaDriverEntryPointSymbolNotFound;
+        if (cudaGetDriverEntryPointByVersion("cuTensorMapEncodeTiled", &fn, 12000, cudaEnableDefault, &q) !=
+                cudaSuccess ||
+            q != cudaDriverEntryPointSuccess)
+            fn = nullptr;
+        return reinterpret_cast<PFN_cuTensorMapEncodeTiled_v12000>(fn);
+    }();
+    return encode;
+}
+
+// A cache as a [rows][n_kv][hd] fp32 tensor map (no swizzle, no multicast)
+// whose boxes are T rows of one KV head.  False when it cannot be encoded.
+bool CacheMap(const float* base, int hd, int n_kv, long long rows, int T, CUtensorMap& map) {
+    std::memset(&map, 0, sizeof(map));
+    const PFN_cuTensorMapEncodeTiled_v12000 encode = TensorMapEncoder();
+    if (!encode) return false;
+    const cuuint64_t gdim[3] = {cuuint64_t(hd), cuuint64_t(n_kv), cuuint64_t(rows)};
+    const cuuint64_t gstride[2] = {cuuint64_t(hd) * 4, cuuint64_t(n_kv) * hd * 4};
+    const cuuint32_t box[3] = {cuuint32_t(hd), 1, cuuint32_t(T)};
+    const cuuint32_t estride[3] = {1, 1, 1};
+    return encode(&map, CU_TENSOR_MAP_DATA_TYPE_FLOAT32, 3, const_cast<float*>(base), gdim, gstride, box, estride,
+                  CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_NONE, CU_TENSOR_MAP_L2_PROMOTION_L2_256B,
+                  CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE) == CUDA_SUCCESS;
+}
+
+template <int GM, bool TMA>
+void LaunchAttnT(const AttnParams& p, int batch, cudaStream_t stream, bool pdl, const CUtensorMap& km,
+                 const CUtensorMap& vm) {
+    const size_t smem = AttnSmemBytes(p.hd, GM);
     static int configured[64] = {};
     int dev = 0;
     CheckCuda(cudaGetDevice(&dev), "cudaGetDevice");
     if (dev >= 64 || configured[dev] < static_cast<int>(smem)) {
-        CheckCuda(cudaFuncSetAttribute(AttnSplitKernel<DPL>,
-                                       cudaFuncAttributeMaxDynamicSharedMemorySize,
+        CheckCuda(cudaFuncSetAttribute(AttnSplitKernel<GM, TMA>, cudaFuncAttributeMaxDynamicSharedMemorySize,
                                        static_cast<int>(smem)),
                   "cudaFuncSetAttribute(AttnSplitKernel)");
         if (dev < 64) configured[dev] = static_cast<int>(smem);
     }
     dim3 grid(p.n_kv * p.hgroups, p.chunks, batch);
-    Launch("AttnSplitKernel", AttnSplitKernel<DPL>, grid, dim3(kAttnThreads), smem, stream, pdl, p);
+    Launch("AttnSplitKernel", AttnSplitKernel<GM, TMA>, grid, dim3(kAttnThreads), smem, stream, pdl, p, km, vm);
 }
 
+template <bool TMA>
+void LaunchAttnG(const AttnParams& p, int batch, cudaStream_t stream, bool pdl, const CUtensorMap& km,
+                 const CUtensorMap& vm) {
+    const int g = std::min(p.group, kAttnGmax);
+    if (g <= 1) return LaunchAttnT<1, TMA>(p, batch, stream, pdl, km, vm);
+    if (g <= 2) return LaunchAttnT<2, TMA>(p, batch, stream, pdl, km, vm);
+    if (g <= 4) return LaunchAttnT<4, TMA>(p, batch, stream, pdl, km, vm);
+    if (g <= 8) return LaunchAttnT<8, TMA>(p, batch, stream, pdl, km, vm);
+    return LaunchAttnT<16, TMA>(p, batch, stream, pdl, km, vm);
+}
+
+}  // namespace
+
 void LaunchAttention(const AttnParams& p, int batch, cudaStream_t stream, bool pdl) {
-    const int dpl = (p.hd + 31) / 32;
-    if (dpl <= 1) return LaunchAttnT<1>(p, batch, stream, pdl);
-    if (dpl <= 2) return LaunchAttnT<2>(p, batch, stream, pdl);
-    if (dpl <= 4) return LaunchAttnT<4>(p, batch, stream, pdl);
-    if (dpl <= 8) return LaunchAttnT<8>(p, batch, stream, pdl);
-    Fail(MLB_ERR_UNSUPPORTED, "attention: head_dim above 256 is not supported");
+    if (p.hd < 1 || p.hd > 256) Fail(MLB_ERR_UNSUPPORTED, "attention: head_dim above 256 is not supported");
+    AttnParams a = p;
+    const AttnGeom G = AttnGeometry(p.hd);
+    const size_t pstride = size_t(p.n_kv) * p.hd;
+    // Tile copies as tensor-map boxes when rows are whole 16-byte pieces and
+    // the caches are 16-byte aligned; the maps span the rows this launch can
+    // reach: every sequence's layers up to `layer`.
+    bool tma = (p.hd & 3) == 0 &&
+               ((reinterpret_cast<uintptr_t>(p.kc) | reinterpret_cast<uintptr_t>(p.vc)) & 15) == 0 &&
+               p.seq_stride % pstride == 0;
+    CUtensorMap km, vm;
+    std::memset(&km, 0, sizeof(km));
+    std::memset(&vm, 0, sizeof(vm));
+    if (tma) {
+        const long long seq_rows = static_cast<long long>(p.seq_stride / pstride);
+        const long long rows = (p.seq_stride ? (batch - 1) * seq_rows : 0) + (p.layer + 1LL) * p.max_seq_len;
+        tma = seq_rows < (1LL << 30) && rows + G.T < (1LL << 31) && CacheMap(p.kc, p.hd, p.n_kv, rows, G.T, km) &&
+              CacheMap(p.vc, p.hd, p.n_kv, rows, G.T, vm);
+        a.seq_rows = static_cast<int>(seq_rows);
+    }
+    if (tma) LaunchAttnG<true>(a, batch, stream, pdl, km, vm);
+    else LaunchAttnG<false>(a, batch, stream, pdl, km, vm);
+}
+
+void LaunchAttnMerge(const float* part_ml, const float* part_o, int chunks, int hd, float* out, int rows,
+                     cudaStream_t stream) {
+    AttnMergeKernel<<<rows, kAttnMergeThreads, 0, stream>>>(part_ml, part_o, chunks, hd, out);
+    CheckCuda(cudaGetLastError(), "AttnMergeKernel");
 }
 
 namespace {
@@ -79,6 +220,7 @@ void AttentionDecode(const char* caller, int device, int batch, const float* q, 
     p.pos_host = pos;
     p.chunks = AttnChunks(pos + 1, batch, n_kv_heads, p.hgroups, c.sm_count);
     p.out = out;
+    p.status = c.status;
     if (p.chunks > 1) {
         const size_t rows = size_t(batch) * n_heads * p.chunks;
         float* ws = static_cast<float*>(Workspace(c, rows * (head_dim + 2) * sizeof(float)));
@@ -87,9 +229,7 @@ void AttentionDecode(const char* caller, int device, int batch, const float* q, 
     }
     LaunchAttention(p, batch, c.stream, false);
     if (p.chunks > 1) {
-        AttnMergeKernel<<<batch * n_heads, 128, 0, c.stream>>>(p.part_ml, p.part_o, p.chunks,
-                                                               head_dim, out);
-        CheckCuda(cudaGetLastError(), "AttnMergeKernel");
+        LaunchAttnMerge(p.part_ml, p.part_o, p.chunks, head_dim, out, batch * n_heads, c.stream);
     }
 }
 
@@ -132,11 +272,11 @@ int mlb_attention_decode_batched(int device, int batch, const float* q, const fl
 // memory, or a host thread that must not take the allocator's locks or risk
 // the implicit device synchronisation that freeing memory can cause.  For
 // them this entry point keeps the split-K partials in one fixed array that is
-// part of the library image (kNoAllocScratchFloats floats = 16 MiB on every
+// part of the library image (kNoAllocScratchFloats floats = 4 MiB on every
 // device that loads the library, held until the process exits).
 namespace {
 
-constexpr size_t kNoAllocScratchFloats = size_t(4) << 20;  // 16 MiB
+constexpr size_t kNoAllocScratchFloats = size_t(1) << 20;  // 4 MiB
 __device__ __align__(256) float g_noalloc_scratch[kNoAllocScratchFloats];
 
 std::mutex g_noalloc_mutex;
@@ -193,6 +333,7 @@ extern "C" int mlb_attention_decode_noalloc(int device, const float* q, const fl
         p.pos_host = pos;
         p.chunks = AttnChunks(pos + 1, 1, n_kv_heads, p.hgroups, c.sm_count);
         p.out = out;
+        p.status = c.status;
         if (p.chunks > 1) {
             const size_t rows = size_t(n_heads) * p.chunks;
             const size_t need = rows * (head_dim + 2);
@@ -210,9 +351,7 @@ extern "C" int mlb_attention_decode_noalloc(int device, const float* q, const fl
         }
         LaunchAttention(p, 1, c.stream, false);
         if (p.chunks > 1) {
-            AttnMergeKernel<<<n_heads, 128, 0, c.stream>>>(p.part_ml, p.part_o, p.chunks, head_dim,
-                                                            out);
-            CheckCuda(cudaGetLastError(), "AttnMergeKernel");
+            LaunchAttnMerge(p.part_ml, p.part_o, p.chunks, head_dim, out, n_heads, c.stream);
         }
     });
 }

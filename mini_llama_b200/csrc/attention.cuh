@@ -1,21 +1,40 @@
-// Split-K GQA decode attention.
+// Split-K GQA decode attention over the fp32 KV cache.
 //
 // One CTA = (KV head, group of <= kAttnGmax query heads sharing it, chunk of
-// <= kAttnChunk positions, sequence).  The CTA stages q of its heads and the K
-// and V rows of its chunk in shared memory with asynchronous copies (one
-// memory round trip; each K/V row is read once for all query heads of the
-// group).  Warps then take (query head, 32-position tile) items: a lane per
-// position scores its key (K rows at stride hd+1, conflict-free), the warp
-// forms the tile's softmax (max, sum), and a lane per head dimension
-// accumulates the probability-weighted V rows.  The tiles of a head merge in
-// shared memory; with one chunk the CTA writes the normalised output,
-// otherwise (m, l, o) partials that a merge step (a small kernel, or the
-// O-projection GEMV prologue in the decode graph) combines.
+// positions, sequence).  The chunk is streamed through shared memory in tiles
+// of T rows (T x padded head_dim = kAttnStageFloats, e.g. 32 rows of 128
+// floats: 16 KB of K and 16 KB of V a tile) by a ring of kAttnStages stages,
+// kAttnStages - 1 tiles ahead of the one being computed, so a CTA keeps two
+// tiles in flight while it works.  A tile is two tensor-map boxes (TMA, one
+// for K and one for V, completing on the stage's mbarrier) when head_dim is a
+// multiple of 4 and the caches are 16-byte aligned; otherwise single-float
+// cp.async copies.  Per tile:
+//   scores   256 / T threads per position (consecutive lanes), each over a
+//            quarter or less of the row's 16-byte pieces, every query head of
+//            the group at once (q in shared memory, one dot per head in
+//            registers), summed over the position's lanes by shuffles
+//   softmax  a warp per head: the tile's maximum, the running maximum and sum
+//            (online softmax across tiles), the tile's weights in place
+//   values   a thread per (16-byte column, row group): o[head] += w x V row
+//            for every head (V read once for all heads), scaled by the
+//            running-maximum correction first
+// Each row of K is read once for all query heads of its group and each tile
+// costs three CTA barriers.  At the end the row groups' partial outputs are
+// summed in shared memory: with one chunk the CTA writes the normalised
+// output, otherwise (m, l, o) partials that a merge step (AttnMergeKernel, or
+// the O-projection GEMV prologue in the decode graph) combines.
+//
+// The grid is sized by AttnChunks: short contexts split into chunks of at
+// least 16 positions while the grid is below two waves; long contexts into as
+// few chunks as fill kAttnCtasPerSm CTAs per SM, so the K/V bytes stream
+// through long-running CTAs and the partials stay small.
 //
 // Replaces AttentionScoresKernel + AttentionReduceKernel (mini_llama
 // src/cuda_attention.cu:87-181): one CTA per (head, position), a global score
 // scratch, expf recomputed per (dim, position) and two device syncs.
 #pragma once
+
+#include <cuda.h>
 
 #include "common.cuh"
 
@@ -23,9 +42,11 @@ namespace mlb {
 
 constexpr int kAttnThreads = 256;
 constexpr int kAttnWarps = kAttnThreads / 32;
-constexpr int kAttnGmax = 16;   // query heads of one KV group handled by one CTA
-constexpr int kAttnTile = 32;   // positions per warp item (one per lane)
-constexpr int kAttnChunk = 64;  // positions per CTA (K and V of the chunk sit in shared memory)
+constexpr int kAttnGmax = 16;           // query heads of one KV group handled by one CTA
+constexpr int kAttnStages = 3;          // K/V tiles in the shared-memory ring
+constexpr int kAttnStageFloats = 4096;  // tile rows x padded head_dim (rounded up to a power of two)
+constexpr int kAttnCtasPerSm = 2;       // resident CTAs per SM the long-context grid is sized for
+constexpr int kAttnPieces = 4;          // 16-byte pieces of a row one score thread covers at most
 
 struct AttnParams {
     // query source: q[b][h][hd] (stride q_batch_stride per sequence)
@@ -41,7 +62,7 @@ struct AttnParams {
     int hd;
     int group;    // n_heads / n_kv
     int hgroups;  // ceil(group / kAttnGmax)
-    int chunks;   // position chunks; chunks * kAttnChunk >= positions + 1
+    int chunks;   // position chunks (any count >= 1; a CTA loops over its chunk's tiles)
     float scale;
     // positions: pos_dev ? pos_dev[b * pos_stride] : pos_host
     const int* pos_dev;
@@ -59,195 +80,86 @@ struct AttnParams {
     const float* rope_cos;  // [max_seq_len][hd/2]
     const float* rope_sin;
     int neox;
+    // device status word: a tile copy that does not arrive within
+    // kAttnWaitNs records MLB_ERR_DEVICE_TIMEOUT here (tensor-map path)
+    int* status;
+    // tensor-map path: cache rows of sequence b, layer `layer` start at row
+    // b * seq_rows + layer * max_seq_len of the [rows][n_kv][hd] maps
+    int seq_rows;
 };
 
-__host__ __device__ inline size_t AttnSmemBytes(int hd) {
-    const int items = kAttnGmax * (kAttnChunk / kAttnTile);
-    return (size_t(kAttnGmax) * hd +                  // q
-            size_t(kAttnChunk) * (hd + 1) +            // K rows (stride hd+1: lane per position)
-            size_t(kAttnChunk) * hd +                  // V rows
-            size_t(items) * (hd + 2)) * 4;             // per-item (m, l, o)
+constexpr uint64_t kAttnWaitNs = 2000000000ull;  // bound of one tile wait
+
+// Tile geometry of a head_dim (the same on host and device).
+struct AttnGeom {
+    int hdp;  // head_dim rounded up to a multiple of 4 (row stride in shared memory)
+    int lpr;  // 16-byte pieces per row (hdp / 4)
+    int T;    // rows per tile
+    int tpp;  // score threads per position (kAttnThreads / T)
+    int R;    // row groups of the value pass (kAttnThreads / lpr)
+    // K rows are stored as they are; the score thread of row r takes its
+    // pieces ssub + tpp i in the order i ^ (((r >> ksh) & kmk) * kml / tpp),
+    // which puts the eight threads of a shared-memory phase on eight distinct
+    // bank groups
+    int ksh, kmk, kml;
+};
+
+__host__ __device__ inline AttnGeom AttnGeometry(int hd) {
+    AttnGeom g;
+    g.hdp = (hd + 3) & ~3;
+    g.lpr = g.hdp / 4;
+    int p2 = 4;
+    while (p2 < g.hdp) p2 <<= 1;
+    g.T = kAttnStageFloats / p2 < kAttnThreads ? kAttnStageFloats / p2 : kAttnThreads;
+    g.tpp = kAttnThreads / g.T;
+    g.R = kAttnThreads / g.lpr;
+    g.ksh = g.kmk = g.kml = 0;
+    if ((g.lpr & (g.lpr - 1)) == 0) {
+        if (g.lpr >= 8 && g.tpp < 8) {  // rows of 8+ pieces: a phase spans 8 / tpp rows
+            g.kmk = 8 / g.tpp - 1;
+            g.kml = g.tpp;
+        } else if (g.lpr < 8) {  // one thread per row, 8 / lpr rows per 128 bytes
+            g.ksh = g.lpr == 4 ? 1 : (g.lpr == 2 ? 2 : 3);
+            g.kmk = g.lpr - 1;
+            g.kml = 1;
+        }
+    }
+    return g;
 }
 
-template <int DPL>
-__global__ void __launch_bounds__(kAttnThreads) AttnSplitKernel(const AttnParams p) {
-    extern __shared__ __align__(16) float asmem[];
-    const int hd = p.hd;
-    const int krow = hd + 1;
-    float* qs = asmem;                         // [G][hd]
-    float* ks = qs + kAttnGmax * hd;           // [chunk][hd+1]
-    float* vs = ks + kAttnChunk * krow;        // [chunk][hd]
-    float* res = vs + kAttnChunk * hd;         // [items][hd+2]: m, l, o[hd]
+// Shared memory of the kernel for (head_dim, heads per CTA GM): a 128-byte
+// header (the stages' mbarriers, the abort flag), then floats: the ring (its
+// space holds the row groups' partial outputs after the loop), q of the
+// group, this token's k and v rows, the tile's scores, three per-head
+// scalars.
+constexpr int kAttnHeader = 128;
 
-    const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
-    const int kvh = blockIdx.x / p.hgroups, hg = blockIdx.x % p.hgroups;
-    const int chunk = blockIdx.y, b = blockIdx.z;
-    const int h0 = kvh * p.group + hg * kAttnGmax;
-    const int gcnt = min(kAttnGmax, p.group - hg * kAttnGmax);
-
-    GridDepWait();
-    GridDepLaunch();
-
-    // A position outside the cache (possible only through a device array)
-    // attends to nothing and yields zeros instead of reading out of bounds.
-    const int pos_raw = p.pos_dev ? p.pos_dev[size_t(b) * p.pos_stride] : p.pos_host;
-    const bool valid = pos_raw >= 0 && pos_raw < p.max_seq_len;
-    const int pos = valid ? pos_raw : 0;
-    const int npos = valid ? pos_raw + 1 : 0;
-    const int clen = min(kAttnChunk, (npos + p.chunks - 1) / p.chunks);
-    const int p0 = min(npos, chunk * clen), p1 = min(npos, p0 + clen);
-    const int len = p1 - p0;
-    const bool own_new = p.fused_rope && valid && pos >= p0 && pos < p1;
-
-    const size_t pos_stride = size_t(p.n_kv) * hd;
-    float* kbase = p.kc + size_t(b) * p.seq_stride + size_t(p.layer) * p.max_seq_len * pos_stride +
-                   size_t(kvh) * hd;
-    float* vbase = p.vc + size_t(b) * p.seq_stride + size_t(p.layer) * p.max_seq_len * pos_stride +
-                   size_t(kvh) * hd;
-
-    // ---- q of the group, and K/V of the chunk, into shared memory
-    const float* qsrc = p.q + size_t(b) * p.q_batch_stride + size_t(h0) * hd;
-    for (int i = threadIdx.x; i < gcnt * hd; i += kAttnThreads) CpAsync4(qs + i, qsrc + i);
-    for (int i = threadIdx.x; i < len * hd; i += kAttnThreads) {
-        const int r = i / hd, d = i - r * hd;
-        if (own_new && p0 + r == pos) continue;  // this token's row comes from kv_new below
-        CpAsync4(ks + r * krow + d, kbase + size_t(p0 + r) * pos_stride + d);
-        CpAsync4(vs + r * hd + d, vbase + size_t(p0 + r) * pos_stride + d);
-    }
-    CpAsyncWaitAll();
-    __syncthreads();
-    if (p.fused_rope && valid) {
-        // RoPE with the reference CPU tables; the chunk holding `pos` also
-        // rotates this token's k and stores k, v into the cache.
-        const int half = hd / 2;
-        const float* ct = p.rope_cos + size_t(pos) * half;
-        const float* st = p.rope_sin + size_t(pos) * half;
-        for (int i = threadIdx.x; i < gcnt * half; i += kAttnThreads) {
-            const int g = i / half, j = i - g * half;
-            const int a = p.neox ? j : 2 * j, c2 = p.neox ? j + half : 2 * j + 1;
-            const float x0 = qs[g * hd + a], x1 = qs[g * hd + c2], cs = ct[j], sn = st[j];
-            qs[g * hd + a] = __fsub_rn(__fmul_rn(x0, cs), __fmul_rn(x1, sn));
-            qs[g * hd + c2] = __fadd_rn(__fmul_rn(x0, sn), __fmul_rn(x1, cs));
-        }
-        if (own_new) {
-            const float* kn = p.kv_new + size_t(b) * p.kv_batch_stride + size_t(kvh) * hd;
-            const float* vn = (p.v_new ? p.v_new + size_t(b) * p.kv_batch_stride
-                                       : p.kv_new + size_t(b) * p.kv_batch_stride + size_t(p.n_kv) * hd) +
-                              size_t(kvh) * hd;
-            float* kd = kbase + size_t(pos) * pos_stride;
-            float* vd = vbase + size_t(pos) * pos_stride;
-            const int r = pos - p0;
-            for (int j = threadIdx.x; j < half; j += kAttnThreads) {
-                const int a = p.neox ? j : 2 * j, c2 = p.neox ? j + half : 2 * j + 1;
-                const float x0 = kn[a], x1 = kn[c2], cs = ct[j], sn = st[j];
-                const float ka = __fsub_rn(__fmul_rn(x0, cs), __fmul_rn(x1, sn));
-                const float kb = __fadd_rn(__fmul_rn(x0, sn), __fmul_rn(x1, cs));
-                kd[a] = ka;
-                kd[c2] = kb;
-                ks[r * krow + a] = ka;
-                ks[r * krow + c2] = kb;
-            }
-            for (int d = threadIdx.x; d < hd; d += kAttnThreads) {
-                const float v = vn[d];
-                vd[d] = v;
-                vs[r * hd + d] = v;
-            }
-        }
-        __syncthreads();
-    }
-
-    // ---- items: (query head, 32-position tile); lane = position for the
-    // scores, lane = head dimension for the weighted sum of V
-    const int ntile = (len + kAttnTile - 1) / kAttnTile;
-    for (int item = warp; item < gcnt * ntile; item += kAttnWarps) {
-        const int g = item / ntile, tile = item - g * ntile;
-        const int r0 = tile * kAttnTile;
-        const int tn = min(kAttnTile, len - r0);
-        const float* qh = qs + g * hd;
-        float s = -INFINITY;
-        if (lane < tn) {
-            const float* kr = ks + (r0 + lane) * krow;
-            float acc = 0.0f;
-            for (int d = 0; d < hd; ++d) acc = fmaf(qh[d], kr[d], acc);
-            s = acc * p.scale;
-        }
-        const float mt = WarpMax(s);
-        const float pv = lane < tn ? expf(s - mt) : 0.0f;
-        const float lt = WarpSum(pv);
-        float o[DPL];
-#pragma unroll
-        for (int j = 0; j < DPL; ++j) o[j] = 0.0f;
-        for (int r = 0; r < tn; ++r) {
-            const float pr = __shfl_sync(0xffffffffu, pv, r);
-            const float* vr = vs + (r0 + r) * hd;
-#pragma unroll
-            for (int j = 0; j < DPL; ++j) {
-                const int d = lane + 32 * j;
-                if (d < hd) o[j] = fmaf(pr, vr[d], o[j]);
-            }
-        }
-        float* rr = res + item * (hd + 2);
-        if (lane == 0) {
-            rr[0] = mt;
-            rr[1] = lt;
-        }
-#pragma unroll
-        for (int j = 0; j < DPL; ++j) {
-            const int d = lane + 32 * j;
-            if (d < hd) rr[2 + d] = o[j];
-        }
-    }
-    __syncthreads();
-
-    // ---- merge the tiles of each head: final output or the chunk's partial
-    for (int i = threadIdx.x; i < gcnt * hd; i += kAttnThreads) {
-        const int g = i / hd, d = i - g * hd;
-        float mx = -INFINITY;
-        for (int tl = 0; tl < ntile; ++tl) mx = fmaxf(mx, res[(g * ntile + tl) * (hd + 2)]);
-        float num = 0.0f, den = 0.0f;
-        for (int tl = 0; tl < ntile; ++tl) {
-            const float* rr = res + (g * ntile + tl) * (hd + 2);
-            const float wt = expf(rr[0] - mx);
-            den = fmaf(wt, rr[1], den);
-            num = fmaf(wt, rr[2 + d], num);
-        }
-        const int h = h0 + g;
-        if (p.chunks == 1) {
-            p.out[(size_t(b) * p.n_heads + h) * hd + d] = den > 0.0f ? num / den : 0.0f;
-        } else {
-            const size_t pc = (size_t(b) * p.n_heads + h) * p.chunks + chunk;
-            p.part_o[pc * hd + d] = num;
-            if (d == 0) {
-                p.part_ml[pc * 2] = ntile ? mx : -INFINITY;
-                p.part_ml[pc * 2 + 1] = den;
-            }
-        }
-    }
+__host__ __device__ inline size_t AttnSmemBytes(int hd, int gm) {
+    const AttnGeom g = AttnGeometry(hd);
+    const size_t ring = size_t(2) * kAttnStages * g.T * g.hdp;
+    const size_t red = size_t(g.R) * gm * g.hdp;
+    return kAttnHeader + ((ring > red ? ring : red) + size_t(gm) * g.hdp + 2 * size_t(g.hdp) +
+                          size_t(gm) * g.T + 3 * size_t(gm)) * 4;
 }
 
-// out[b][h][d] = sum_c e^(m_c - M) o_c[d] / sum_c e^(m_c - M) l_c
-static __global__ void AttnMergeKernel(const float* part_ml, const float* part_o, int chunks, int hd,
-                                float* out) {
-    GridDepWait();
-    GridDepLaunch();
-    const size_t bh = blockIdx.x;  // b * n_heads + h
-    const float* ml = part_ml + bh * chunks * 2;
-    float mx = -INFINITY;
-    for (int c = 0; c < chunks; ++c) mx = fmaxf(mx, ml[2 * c]);
-    for (int d = threadIdx.x; d < hd; d += blockDim.x) {
-        float num = 0.0f, den = 0.0f;
-        for (int c = 0; c < chunks; ++c) {
-            float mc = ml[2 * c];
-            if (mc == -INFINITY) continue;
-            float wt = expf(mc - mx);
-            den = fmaf(wt, ml[2 * c + 1], den);
-            num = fmaf(wt, part_o[(bh * chunks + c) * hd + d], num);
-        }
-        out[bh * hd + d] = den > 0.0f ? num / den : 0.0f;
-    }
+__device__ __forceinline__ void CpAsyncCommit() { asm volatile("cp.async.commit_group;" ::: "memory"); }
+
+template <int N>
+__device__ __forceinline__ void CpAsyncWaitGroup() {
+    asm volatile("cp.async.wait_group %0;" ::"n"(N) : "memory");
 }
 
-void LaunchAttention(const AttnParams& p, int batch, cudaStream_t stream, bool pdl);
-int AttnChunks(int max_npos, int batch, int n_kv, int hgroups, int sm_count);
+__device__ __forceinline__ float4 Lds4(const float* p) { return *reinterpret_cast<const float4*>(p); }
+
+// One 3-D tensor-map box (no multicast) into shared memory, completing on bar.
+__device__ __forceinline__ void TmaLoad3D(void* dst, const CUtensorMap* map, int x, int y, int z, uint64_t* bar) {
+    asm volatile(
+        "cp.async.bulk.tensor.3d.shared::cluster.global.mbarrier::complete_tx::bytes [%0], [%1, {%2, %3, %4}], "
+        "[%5];" ::"r"(SmemAddr(dst)),
+        "l"(reinterpret_cast<uint64_t>(map)), "r"(x), "r"(y), "r"(z), "r"(SmemAddr(bar))
+        : "memory");
+}
 
 }  // namespace mlb
+
+#include "attention_kernel.cuh"

@@ -306,10 +306,10 @@ void CaptureBatchStep(mlb_batch* s, DeviceContext& c) {
                 a.rope_cos = m->rope_cos;
                 a.rope_sin = m->rope_sin;
                 a.neox = cf.rope_type == MLB_ROPE_NEOX;
+                a.status = status;
                 LaunchAttention(a, B, st, true);
                 if (s->chunks > 1) {
-                    AttnMergeKernel<<<B * nh, 128, 0, st>>>(s->part_ml, s->part_o, s->chunks, hd, s->attn_l);
-                    CheckCuda(cudaGetLastError(), "AttnMergeKernel");
+                    LaunchAttnMerge(s->part_ml, s->part_o, s->chunks, hd, s->attn_l, B * nh, st);
                 }
             }
             // 3. whole attention rows -> this rank's wo rows -> x_mid = x + all rows

@@ -337,6 +337,7 @@ void CaptureStep(mlb_session* s, DeviceContext& c) {
                 a.rope_cos = m->rope_cos;
                 a.rope_sin = m->rope_sin;
                 a.neox = cf.rope_type == MLB_ROPE_NEOX;
+                a.status = status;
                 LaunchAttention(a, 1, st, true);
             }
             // 3. O projection + residual
@@ -650,10 +651,10 @@ void Prefill(mlb_session* s, DeviceContext& c, int start, int n) {
         a.part_ml = s->pf_part_ml;
         a.part_o = s->pf_part_o;
         a.fused_rope = 0;
+        a.status = status;
         LaunchAttention(a, n, st, true);
         if (chunks > 1) {
-            AttnMergeKernel<<<n * cf.n_heads, 128, 0, st>>>(s->pf_part_ml, s->pf_part_o, chunks, hd, s->pf_attn);
-            CheckCuda(cudaGetLastError(), "AttnMergeKernel");
+            LaunchAttnMerge(s->pf_part_ml, s->pf_part_o, chunks, hd, s->pf_attn, n * cf.n_heads, st);
         }
         linear(s->pf_attn, W(l, MLB_W_WO), n, qd, D, nullptr, s->pf_o);
         add(s->pf_x, s->pf_o, s->pf_xmid, size_t(n) * D);

@@ -14,6 +14,11 @@ namespace {
 thread_local std::string g_last_error;
 std::mutex g_ctx_mutex;
 std::vector<DeviceContext*> g_ctx;
+// The op kernels' device status words: part of the library image (every
+// device that loads the library holds its own copy, zero at load), so setting
+// up a device allocates no device memory.  Word 0 is the status the op
+// kernels set and mlb_synchronize reads.
+__device__ __align__(256) int g_status_words[64];
 }  // namespace
 
 void SetLastError(const std::string& msg) { g_last_error = msg; }
@@ -48,8 +53,9 @@ DeviceContext& Ctx(int device) {
         uint64_t keep = UINT64_MAX;  // never hand freed blocks back to the driver
         CheckCuda(cudaMemPoolSetAttribute(c->pool, cudaMemPoolAttrReleaseThreshold, &keep),
                   "cudaMemPoolSetAttribute");
-        CheckCuda(cudaMalloc(&c->status, 256), "cudaMalloc(status)");
-        CheckCuda(cudaMemset(c->status, 0, 256), "cudaMemset(status)");
+        void* st = nullptr;  // this device's copy of g_status_words (the device is current)
+        CheckCuda(cudaGetSymbolAddress(&st, g_status_words), "cudaGetSymbolAddress(status)");
+        c->status = static_cast<int*>(st);
         g_ctx[device] = c;
     }
     return *g_ctx[device];

@@ -46,10 +46,11 @@ def test_noalloc_attention_matches_allocating_entry_point(mlb, gpu, oracle):
 
 
 def test_noalloc_attention_rejects_oversized_scratch(mlb, gpu):
-    # 64 heads of 256 at 32768 positions need more partials than the array holds;
-    # the shape check happens before any device work
+    # 64 heads of 256 over 4 KV heads at 32768 positions split into 74 chunks:
+    # 64 x 74 x 258 partial floats, more than the array's 1 Mi; the shape
+    # check happens before any device work
     q = DeviceArray(mlb, gpu, 64)
     st = mlb.raw("mlb_attention_decode_noalloc", gpu, q.ptr, q.ptr, q.ptr, 1, 32768, 0, 32767,
-                 64, 8, 256, q.ptr)
+                 64, 4, 256, q.ptr)
     assert st == capi.MLB_ERR_UNSUPPORTED
     assert "split-K scratch" in mlb.last_error()
