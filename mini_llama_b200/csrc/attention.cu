@@ -77,8 +77,19 @@ __global__ void __launch_bounds__(kAttnMergeThreads) AttnMergeKernel(const float
             den = fmaf(w, ml[2 * (c0 + c) + 1], den);
         }
         __syncthreads();
-        if (sl < nsl)
-            for (int c = sl; c < cn; c += nsl) num = fmaf(wt[c], po[size_t(c0 + c) * hd + d], num);
+        if (sl < nsl) {
+            // eight partial rows in flight per thread (independent loads,
+            // then the weighted sum)
+            int c = sl;
+            for (; c + 7 * nsl < cn; c += 8 * nsl) {
+                float v[8];
+#pragma unroll
+                for (int k = 0; k < 8; ++k) v[k] = po[size_t(c0 + c + k * nsl) * hd + d];
+#pragma unroll
+                for (int k = 0; k < 8; ++k) num = fmaf(wt[c + k * nsl], v[k], num);
+            }
+            for (; c < cn; c += nsl) num = fmaf(wt[c], po[size_t(c0 + c) * hd + d], num);
+        }
     }
     den = WarpSum(den);
     __syncthreads();

@@ -220,7 +220,7 @@ __global__ void __launch_bounds__(kAttnThreads, 2)
 #pragma unroll
             for (int g = 0; g < GM; ++g) dot[g] = 0.0f;
             const float* krow = r0 + sr == skip_row ? kn : kt + sr * hdp;
-#pragma unroll 1
+#pragma unroll 2
             for (int i = 0; i < kAttnPieces; ++i) {
                 const int c = ssub + tpp * (i ^ sperm);
                 if (c < lpr) {
