@@ -283,6 +283,24 @@ def test_attention_sweep(mlb, gpu, oracle, golden_ops, shape):
         stream += 8
 
 
+@pytest.mark.parametrize("shape", [
+    (32, 1, 64, 300),   # 32 query heads on one KV head: two head groups of 16 per KV head
+    (12, 4, 96, 257),   # head_dim 96: rows of 24 pieces, strided value rows
+    (8, 8, 256, 100),   # head_dim 256: 16-row tiles
+    (6, 2, 20, 70),     # head_dim 20: five pieces per row, two score threads per position
+    (4, 1, 8, 40),      # head_dim 8: 256-row tiles, a thread per position
+    (7, 7, 30, 33),     # head_dim 30: single-float copies, padded rows
+])
+def test_attention_tile_geometries(mlb, gpu, oracle, shape):
+    """Every tile geometry of the split-K kernel (rows per tile, threads per
+    position, value-row layout, head groups) against the oracle."""
+    nh, nkv, hd, pos = shape
+    q, kc, vc = attention_inputs(oracle, 2, 1, pos, nh, nkv, hd, 5000 + nh * 16 + hd, max_seq=pos + 9)
+    got = attention_gpu(mlb, gpu, q, kc, vc, 1, pos, nh, nkv, hd)
+    ref = oracle.attention(q, kc, vc, 1, pos, nh, nkv, hd)
+    assert_close(got, ref, OP_TOL, f"attention {nh}/{nkv}x{hd} pos={pos}")
+
+
 def test_attention_batched_independent_sequences(mlb, gpu, oracle):
     """32 sequences with different lengths in one call equal 32 single calls."""
     batch, nh, nkv, hd, max_seq, layers = 32, 14, 2, 64, 300, 2
