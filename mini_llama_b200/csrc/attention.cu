@@ -1,6 +1,4 @@
 // Decode-attention entry points (replace mini_llama include/cuda_attention.h:10-14).
-#include <cudaTypedefs.h>
-
 #include <algorithm>
 #include <cmath>
 #include <cstring>
@@ -103,21 +101,6 @@ __global__ void __launch_bounds__(kAttnMergeThreads) AttnMergeKernel(const float
         for (int s = 0; s < nsl; ++s) t += sred[s * hd + dd];
         out[bh * hd + dd] = tden > 0.0f ? t / tden : 0.0f;
     }
-}
-
-// The driver's tensor-map encoder through the runtime (the library does not
-// link the driver library); null when the driver does not offer it.
-PFN_cuTensorMapEncodeTiled_v12000 TensorMapEncoder() {
-    static PFN_cuTensorMapEncodeTiled_v12000 encode = [] {
-        void* fn = nullptr;
-        cudaDriverEntryPointQueryResult q = cudaDriverEntryPointSymbolNotFound;
-        if (cudaGetDriverEntryPointByVersion("cuTensorMapEncodeTiled", &fn, 12000, cudaEnableDefault, &q) !=
-                cudaSuccess ||
-            q != cudaDriverEntryPointSuccess)
-            fn = nullptr;
-        return reinterpret_cast<PFN_cuTensorMapEncodeTiled_v12000>(fn);
-    }();
-    return encode;
 }
 
 // A cache as a [rows][n_kv][hd] fp32 tensor map (no swizzle, no multicast)

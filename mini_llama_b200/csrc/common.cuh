@@ -1,6 +1,8 @@
 // Shared device/host helpers of the mini_llama_b200 CUDA library (sm_100a).
 #pragma once
 
+#include <cuda.h>
+#include <cudaTypedefs.h>
 #include <cuda_fp16.h>
 #include <cuda_runtime.h>
 #include <stdint.h>
@@ -76,6 +78,10 @@ void* Workspace(DeviceContext& ctx, size_t bytes);  // stream-ordered, grow-only
 void* PinnedStaging(DeviceContext& ctx, size_t bytes);
 
 inline size_t CeilDiv(size_t a, size_t b) { return (a + b - 1) / b; }
+
+// The driver's tensor-map encoder, reached through the runtime (the library
+// does not link the driver library); null when the driver does not offer it.
+PFN_cuTensorMapEncodeTiled_v12000 TensorMapEncoder();
 
 // Kernel launch with programmatic dependent launch enabled, so a kernel
 // captured behind another may start its independent prologue (weight

@@ -61,6 +61,19 @@ DeviceContext& Ctx(int device) {
     return *g_ctx[device];
 }
 
+PFN_cuTensorMapEncodeTiled_v12000 TensorMapEncoder() {
+    static PFN_cuTensorMapEncodeTiled_v12000 encode = [] {
+        void* fn = nullptr;
+        cudaDriverEntryPointQueryResult q = cudaDriverEntryPointSymbolNotFound;
+        if (cudaGetDriverEntryPointByVersion("cuTensorMapEncodeTiled", &fn, 12000, cudaEnableDefault, &q) !=
+                cudaSuccess ||
+            q != cudaDriverEntryPointSuccess)
+            fn = nullptr;
+        return reinterpret_cast<PFN_cuTensorMapEncodeTiled_v12000>(fn);
+    }();
+    return encode;
+}
+
 void* Workspace(DeviceContext& ctx, size_t bytes) {
     if (bytes <= ctx.workspace_bytes) return ctx.workspace;
     if (ctx.workspace) CheckCuda(cudaFreeAsync(ctx.workspace, ctx.stream), "cudaFreeAsync");

@@ -808,16 +808,7 @@ int WeightMap(const uint8_t* w, int N, int nb, int cta_rows, CUtensorMap& map) {
     const cuuint64_t gstride[1] = {cuuint64_t(P * rowbytes)};
     const cuuint32_t box[2] = {cuuint32_t(TcBlock<QT>::kRawRow), cuuint32_t(cta_rows / P)};
     const cuuint32_t estride[2] = {1, 1};
-    // the driver's encoder through the runtime (the library does not link the driver library)
-    static PFN_cuTensorMapEncodeTiled_v12000 encode = [] {
-        void* fn = nullptr;
-        cudaDriverEntryPointQueryResult q = cudaDriverEntryPointSymbolNotFound;
-        if (cudaGetDriverEntryPointByVersion("cuTensorMapEncodeTiled", &fn, 12000, cudaEnableDefault, &q) !=
-                cudaSuccess ||
-            q != cudaDriverEntryPointSuccess)
-            fn = nullptr;
-        return reinterpret_cast<PFN_cuTensorMapEncodeTiled_v12000>(fn);
-    }();
+    const PFN_cuTensorMapEncodeTiled_v12000 encode = TensorMapEncoder();
     if (!encode) return 0;
     const CUresult r = encode(&map, CU_TENSOR_MAP_DATA_TYPE_UINT8, 2, const_cast<uint8_t*>(w), gdim, gstride, box,
                               estride, CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_NONE,
