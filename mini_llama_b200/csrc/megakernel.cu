@@ -74,8 +74,7 @@ constexpr size_t kOffVdig = kOffVsx + 128;                                // 4 p
 constexpr size_t kOffRed = kOffVdig + Round128(4 * (4 * 32 + 16));        // 2 x 8 warps x 32
 constexpr size_t kOffVec = kOffRed + 2 * 4 * 8 * 32;                      // 512 floats
 constexpr size_t kOffAtt = kOffVec + 4 * 512;                             // 8 warps x 128
-constexpr size_t kOffSc = kOffAtt + 4 * 8 * 128;                          // kMkAttnChunk floats
-constexpr size_t kOffFixedEnd = kOffSc + Round128(4 * kMkAttnChunk);
+constexpr size_t kOffFixedEnd = kOffAtt + 4 * 8 * 128;
 
 struct MkSmem {  // flags[0] is the CTA's abort flag (read by the producer warp too)
     uint8_t* ring;
@@ -90,7 +89,6 @@ struct MkSmem {  // flags[0] is the CTA's abort flag (read by the producer warp 
     float* red;     // [2][8 warps][32 rows], alternating by chunk (RedBuf)
     float* vec;     // [4 * 128] small vectors (g, u / q, k, v, o)
     float* att;     // [8 warps][hd] attention partials
-    float* sc;      // [kMkAttnChunk] scores / weights of a chunk of positions
     float* acc;     // [dim] block-column products of the CTA, flushed by red.add
     float* kst;     // [kst_rows][hd] cached K rows of the attention item's KV head (swizzled)
     float* scratch; // [32]
@@ -1140,7 +1138,6 @@ __global__ void __launch_bounds__(kMkThreads, 1) MegaDecodeKernel(const MegaPara
     s.red = reinterpret_cast<float*>(smem + kOffRed);
     s.vec = reinterpret_cast<float*>(smem + kOffVec);
     s.att = reinterpret_cast<float*>(smem + kOffAtt);
-    s.sc = reinterpret_cast<float*>(smem + kOffSc);
     const size_t vbytes = Round128(4 * size_t(p.dim));
     s.xs = reinterpret_cast<float*>(smem + kOffFixedEnd);
     s.nw = reinterpret_cast<float*>(smem + kOffFixedEnd + vbytes);
