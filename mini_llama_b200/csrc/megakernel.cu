@@ -48,6 +48,9 @@ __device__ __forceinline__ float4 LdCgF4(const float* p) {
     return v;
 }
 
+__device__ __forceinline__ void RedAdd(float* p, float v) {
+    asm volatile("red.global.add.f32 [%0], %1;" ::"l"(p), "f"(v) : "memory");
+}
 
 // Four consecutive floats in one 16-byte vector reduction (p 16-byte aligned).
 __device__ __forceinline__ void RedAdd4(float* p, float4 v) {
@@ -74,7 +77,8 @@ constexpr size_t kOffVdig = kOffVsx + 128;                                // 4 p
 constexpr size_t kOffRed = kOffVdig + Round128(4 * (4 * 32 + 16));        // 2 x 8 warps x 32
 constexpr size_t kOffVec = kOffRed + 2 * 4 * 8 * 32;                      // 512 floats
 constexpr size_t kOffAtt = kOffVec + 4 * 512;                             // 8 warps x 128
-constexpr size_t kOffFixedEnd = kOffAtt + 4 * 8 * 128;
+constexpr size_t kOffSc = kOffAtt + 4 * 8 * 128;                          // kMkAttnChunk floats
+constexpr size_t kOffFixedEnd = kOffSc + Round128(4 * kMkAttnChunk);
 
 struct MkSmem {  // flags[0] is the CTA's abort flag (read by the producer warp too)
     uint8_t* ring;
@@ -89,6 +93,7 @@ struct MkSmem {  // flags[0] is the CTA's abort flag (read by the producer warp 
     float* red;     // [2][8 warps][32 rows], alternating by chunk (RedBuf)
     float* vec;     // [4 * 128] small vectors (g, u / q, k, v, o)
     float* att;     // [8 warps][hd] attention partials
+    float* sc;      // [kMkAttnChunk] scores / weights of a chunk of positions
     float* acc;     // [dim] block-column products of the CTA, flushed by red.add
     float* kst;     // [kst_rows][hd] cached K rows of the attention item's KV head (swizzled)
     float* scratch; // [32]
@@ -205,6 +210,17 @@ __device__ void LoadVecCg(float* dst, const float* src, int n) {
     for (int i = threadIdx.x * 4; i < n; i += 256 * 4) CpAsync16(dst + i, src + i);
 }
 
+__device__ float ConsumerSum(float v, float* scratch) {
+    v = WarpSum(v);
+    const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+    if (lane == 0) scratch[warp] = v;
+    ConsumerBar();
+    float t = 0.0f;
+#pragma unroll
+    for (int w = 0; w < kMkConsumerWarps; ++w) t += scratch[w];
+    ConsumerBar();
+    return t;
+}
 
 // Round to nearest even for |v| < 2^22 (the digit scaling guarantees it):
 // adding 1.5 * 2^23 leaves the rounded integer in the low mantissa bits.
@@ -213,6 +229,17 @@ __device__ __forceinline__ int RoundSmall(float v) {
 }
 
 
+__device__ float ConsumerMax(float v, float* scratch) {
+    v = WarpMax(v);
+    const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+    if (lane == 0) scratch[warp] = v;
+    ConsumerBar();
+    float t = -INFINITY;
+#pragma unroll
+    for (int w = 0; w < kMkConsumerWarps; ++w) t = fmaxf(t, scratch[w]);
+    ConsumerBar();
+    return t;
+}
 
 // RMSNorm of x (n % 32 == 0, in shared memory) straight into the digit planes
 // and block scales of the normalised vector, which is not stored: a thread
@@ -906,18 +933,21 @@ __device__ unsigned Consumers(const MegaParams& p, const MkSmem& s) {
                         }
                         if (i < lpr && r == pos) vpre[i] = reinterpret_cast<const float4*>(vn)[col];
                     }
-                    // softmax of the warp's own 32 positions (its lanes) by
-                    // shuffles; the value rows of a warp are the same 32
-                    // positions, so each weight comes from a lane of the warp
-                    const float mw = WarpMax(sc);  // -inf when none of the 32 is valid
-                    const float wgt = pp <= pos ? expf(sc - mw) : 0.0f;
-                    const float lw = WarpSum(wgt);
+                    const float mc = ConsumerMax(sc, s.scratch);
+                    const float mnew = fmaxf(m_run, mc);
+                    const float corr = m_run == -INFINITY ? 0.0f : expf(m_run - mnew);
+                    const float wgt = pp <= pos ? expf(sc - mnew) : 0.0f;
+                    s.sc[tid] = wgt;
+                    const float lc = ConsumerSum(wgt, s.scratch);  // barriers publish s.sc
+                    l_run = fmaf(l_run, corr, lc);
+                    m_run = mnew;
+                    // weighted V rows of this warp's 32 positions
                     float4 acc = make_float4(0.f, 0.f, 0.f, 0.f);
 #pragma unroll
                     for (int i = 0; i < 16; ++i) {
                         const int r = r0 + i * rpi + rsub;
-                        const float w = __shfl_sync(0xffffffffu, wgt, (i * rpi + rsub) & 31);
                         if (i < lpr && r <= pos) {
+                            const float w = s.sc[r - base];
                             acc.x = fmaf(w, vpre[i].x, acc.x);
                             acc.y = fmaf(w, vpre[i].y, acc.y);
                             acc.z = fmaf(w, vpre[i].z, acc.z);
@@ -938,8 +968,8 @@ __device__ unsigned Consumers(const MegaParams& p, const MkSmem& s) {
 #pragma unroll
                         for (int i = 0; i < 8; ++i) {
                             const int r = r0 + (i0 + i) * rpi + rsub;
-                            const float w = __shfl_sync(0xffffffffu, wgt, ((i0 + i) * rpi + rsub) & 31);
                             if (i0 + i < lpr && r <= pos) {
+                                const float w = s.sc[r - base];
                                 acc.x = fmaf(w, vv[i].x, acc.x);
                                 acc.y = fmaf(w, vv[i].y, acc.y);
                                 acc.z = fmaf(w, vv[i].z, acc.z);
@@ -954,37 +984,17 @@ __device__ unsigned Consumers(const MegaParams& p, const MkSmem& s) {
                         acc.w += __shfl_xor_sync(0xffffffffu, acc.w, off);
                     }
                     if (rsub == 0) reinterpret_cast<float4*>(s.att + warp * hd)[col] = acc;
-                    if (lane == 0) {
-                        s.scratch[2 * warp] = mw;
-                        s.scratch[2 * warp + 1] = lw;
+                    ConsumerBar();
+                    for (int d = tid; d < hd; d += 256) {
+                        float t = 0.0f;
+#pragma unroll
+                        for (int w = 0; w < kMkConsumerWarps; ++w) t += s.att[w * hd + d];
+                        o[d] = fmaf(o[d], corr, t);
                     }
                     ConsumerBar();
-                    // merge of the eight warps' (max, sum, outputs) into the
-                    // running ones, by the threads that own output d
-                    for (int d = tid; d < hd; d += 256) {
-                        float mx = m_run;
-#pragma unroll
-                        for (int w = 0; w < kMkConsumerWarps; ++w) mx = fmaxf(mx, s.scratch[2 * w]);
-                        const float corr = m_run == -INFINITY ? 0.0f : expf(m_run - mx);
-                        float lsum = l_run * corr, t = o[d] * corr;
-#pragma unroll
-                        for (int w = 0; w < kMkConsumerWarps; ++w) {
-                            const float m_w = s.scratch[2 * w];
-                            if (m_w != -INFINITY) {
-                                const float e = expf(m_w - mx);
-                                lsum = fmaf(e, s.scratch[2 * w + 1], lsum);
-                                t = fmaf(e, s.att[w * hd + d], t);
-                            }
-                        }
-                        o[d] = t;
-                        l_run = lsum;
-                        m_run = mx;
-                    }
-                    if (base + kMkAttnChunk <= pos) ConsumerBar();  // s.att and s.scratch are rewritten next pass
                 }
                 // the normalised output's digit planes, straight from the
-                // warps that hold it (warp w: block w; hd is a multiple of 32;
-                // thread d merged o[d] and holds m_run, l_run)
+                // warps that hold it (warp w: block w; hd is a multiple of 32)
                 for (int d = tid; d < hd; d += 256)
                     DigitsWarp(o[d] / l_run, s.vdig + (d >> 5) * 32, vstride, s.vsx + (d >> 5));
                 ConsumerBar();
@@ -1138,6 +1148,7 @@ __global__ void __launch_bounds__(kMkThreads, 1) MegaDecodeKernel(const MegaPara
     s.red = reinterpret_cast<float*>(smem + kOffRed);
     s.vec = reinterpret_cast<float*>(smem + kOffVec);
     s.att = reinterpret_cast<float*>(smem + kOffAtt);
+    s.sc = reinterpret_cast<float*>(smem + kOffSc);
     const size_t vbytes = Round128(4 * size_t(p.dim));
     s.xs = reinterpret_cast<float*>(smem + kOffFixedEnd);
     s.nw = reinterpret_cast<float*>(smem + kOffFixedEnd + vbytes);
