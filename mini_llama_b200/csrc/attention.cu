@@ -38,14 +38,16 @@ int AttnChunks(int max_npos, int batch, int n_kv, int hgroups, int sm_count) {
 namespace {
 
 // out[b][h][d] = sum_c e^(m_c - M) o_c[d] / sum_c e^(m_c - M) l_c, one CTA of
-// kAttnMergeThreads per (sequence, head): the chunk weights once into shared
-// memory (kAttnMergeBatch at a time), then (chunk slice, dimension) threads
-// over the unnormalised outputs, the slices summed at the end.
+// kAttnMergeThreads per (sequence, head, 32 dimensions): the chunk weights
+// once into shared memory (kAttnMergeBatch at a time), then a warp per chunk
+// slice, a lane per dimension, over the unnormalised outputs (eight rows in
+// flight per thread); the slices summed at the end.
 constexpr int kAttnMergeThreads = 256;
 constexpr int kAttnMergeBatch = 1024;
 
 __global__ void __launch_bounds__(kAttnMergeThreads) AttnMergeKernel(const float* part_ml, const float* part_o,
                                                                     int chunks, int hd, float* out) {
+    constexpr int nsl = kAttnWarps;  // chunk slices
     __shared__ float wt[kAttnMergeBatch];
     __shared__ float sred[kAttnMergeThreads];
     __shared__ float sden[kAttnWarps];
@@ -53,6 +55,8 @@ __global__ void __launch_bounds__(kAttnMergeThreads) AttnMergeKernel(const float
     GridDepLaunch();
     const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
     const size_t bh = blockIdx.x;  // b * n_heads + h
+    const int d = blockIdx.y * 32 + lane;
+    const bool dok = d < hd;
     const float* ml = part_ml + bh * chunks * 2;
     const float* po = part_o + bh * chunks * hd;
     float mx = -INFINITY;
@@ -62,8 +66,6 @@ __global__ void __launch_bounds__(kAttnMergeThreads) AttnMergeKernel(const float
     __syncthreads();
     mx = sden[0];
     for (int w = 1; w < kAttnWarps; ++w) mx = fmaxf(mx, sden[w]);
-    const int nsl = hd < kAttnMergeThreads ? kAttnMergeThreads / hd : 1;  // chunk slices
-    const int sl = tid / hd, d = tid - sl * hd;
     float num = 0.0f, den = 0.0f;
     for (int c0 = 0; c0 < chunks; c0 += kAttnMergeBatch) {
         const int cn = min(kAttnMergeBatch, chunks - c0);
@@ -75,10 +77,8 @@ __global__ void __launch_bounds__(kAttnMergeThreads) AttnMergeKernel(const float
             den = fmaf(w, ml[2 * (c0 + c) + 1], den);
         }
         __syncthreads();
-        if (sl < nsl) {
-            // eight partial rows in flight per thread (independent loads,
-            // then the weighted sum)
-            int c = sl;
+        if (dok) {
+            int c = warp;
             for (; c + 7 * nsl < cn; c += 8 * nsl) {
                 float v[8];
 #pragma unroll
@@ -94,12 +94,12 @@ __global__ void __launch_bounds__(kAttnMergeThreads) AttnMergeKernel(const float
     if (lane == 0) sden[warp] = den;
     sred[tid] = num;
     __syncthreads();
-    float tden = 0.0f;
-    for (int w = 0; w < kAttnWarps; ++w) tden += sden[w];
-    for (int dd = tid; dd < hd; dd += kAttnMergeThreads) {
+    if (warp == 0 && dok) {
+        float tden = 0.0f;
+        for (int w = 0; w < kAttnWarps; ++w) tden += sden[w];
         float t = 0.0f;
-        for (int s = 0; s < nsl; ++s) t += sred[s * hd + dd];
-        out[bh * hd + dd] = tden > 0.0f ? t / tden : 0.0f;
+        for (int sl = 0; sl < nsl; ++sl) t += sred[sl * 32 + lane];
+        out[bh * hd + d] = tden > 0.0f ? t / tden : 0.0f;
     }
 }
 
@@ -175,7 +175,7 @@ void LaunchAttention(const AttnParams& p, int batch, cudaStream_t stream, bool p
 
 void LaunchAttnMerge(const float* part_ml, const float* part_o, int chunks, int hd, float* out, int rows,
                      cudaStream_t stream) {
-    AttnMergeKernel<<<rows, kAttnMergeThreads, 0, stream>>>(part_ml, part_o, chunks, hd, out);
+    AttnMergeKernel<<<dim3(rows, (hd + 31) / 32), kAttnMergeThreads, 0, stream>>>(part_ml, part_o, chunks, hd, out);
     CheckCuda(cudaGetLastError(), "AttnMergeKernel");
 }
 
