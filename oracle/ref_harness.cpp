@@ -235,6 +235,14 @@ void CaseAttention() {
                          4, 2, hd, stream);
             stream += 8;
         }
+    // tile geometries of the split-K kernel: (heads, KV heads, head_dim, pos),
+    // 2 layers, layer 1, stream 5000 + 16 heads + head_dim
+    const int geo[6][4] = {{32, 1, 64, 300}, {12, 4, 96, 257}, {8, 8, 256, 100},
+                           {6, 2, 20, 70},   {4, 1, 8, 40},    {7, 7, 30, 33}};
+    for (const auto& g : geo)
+        AttentionOne("geo_" + std::to_string(g[0]) + "x" + std::to_string(g[1]) + "x" + std::to_string(g[2]) +
+                         "_p" + std::to_string(g[3]),
+                     2, 1, g[3], g[0], g[1], g[2], 5000 + 16 * g[0] + g[2]);
     // decode-attention sweep shapes
     for (int shape = 0; shape < 2; ++shape) {
         int nh = shape == 0 ? 14 : 32, nkv = shape == 0 ? 2 : 8, hd = shape == 0 ? 64 : 128;

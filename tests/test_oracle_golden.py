@@ -142,6 +142,9 @@ def attention_case(oracle, layers, layer, pos, nh, nkv, hd, stream):
 ATTN_GRID = [(hd, pos) for hd in (7, 128, 129) for pos in (0, 4, 126, 127, 128, 256)]
 ATTN_SWEEP = [(nh, nkv, hd, pos) for (nh, nkv, hd) in ((14, 2, 64), (32, 8, 128))
               for pos in (127, 1023, 8191, 32767)]
+# shapes that exercise every tile geometry of the device kernel
+ATTN_GEO = [(32, 1, 64, 300), (12, 4, 96, 257), (8, 8, 256, 100), (6, 2, 20, 70), (4, 1, 8, 40),
+            (7, 7, 30, 33)]
 
 
 def test_attention(oracle, golden_ops):
@@ -156,6 +159,10 @@ def test_attention(oracle, golden_ops):
         assert_bits_equal(oracle.attention(q, kc, vc, 0, pos, nh, nkv, hd),
                           golden_ops[f"attn_sweep_{nh}x{hd}_p{pos}"], f"sweep {nh} {hd} {pos}")
         stream += 8
+    for nh, nkv, hd, pos in ATTN_GEO:
+        q, kc, vc = attention_case(oracle, 2, 1, pos, nh, nkv, hd, 5000 + 16 * nh + hd)
+        assert_bits_equal(oracle.attention(q, kc, vc, 1, pos, nh, nkv, hd),
+                          golden_ops[f"attn_geo_{nh}x{nkv}x{hd}_p{pos}"], f"geometry {nh} {nkv} {hd} {pos}")
 
 
 def check_model(oracle, golden, name, prompt_len, n_new, full_logits, max_steps=None):
