@@ -14,10 +14,18 @@ device); --graph selects the CUDA graph per token instead.
   roofline  the dominant kernel: the persistent decode kernel, algorithmic
          bytes of its 128 tokens / its CUDA-event time per launch vs measured
          HBM (graph path: the Q8_0 GEMV timed alone on the lm_head shape)
-  cpu_baseline  the reference CPU implementation (RunBenchmark, built from the
-         reference sources into oracle/_ref) on a bounded sample
+  cpu_baseline  the reference CPU implementation (its RunBenchmark decode loop,
+         built from the reference sources into oracle/_ref) on a bounded
+         sample of the same workload: the 64-token prompt prefilled once,
+         untimed, then steps of 4 greedy tokens continuing from position 64
+  prefill  the 64-token prompt pass alone (mlb_session_generate with one new
+         token): prompt tokens/s
+  dropin the reference's own, unchanged forward.cpp device path linked
+         against this library (oracle/_ref/forward_on_b200): decode tokens/s
+         of 128 greedy tokens after the same prompt
 With N > 1 (torchrun) every GPU decodes its own sequence (replicas; weak scaling).
---impl reference times the reference CPU implementation alone.
+--impl reference times the reference CPU implementation alone, on the same
+config, one line from rank 0.
 """
 from __future__ import annotations
 
@@ -56,6 +64,19 @@ CONFIG = {"workload": "Qwen2-0.5B-arch Q8_0 random-init, batch 1, prompt 64 + 12
           "model": "qwen2-0.5b-arch", "weights": "Q8_0 (lm_head tied, Q8_0)", "global_batch": 1,
           "seq_len": PROMPT + NEW, "decode_tokens_per_step": NEW,
           "l2": "inputs larger than L2 (528 MB of weights streamed per token)"}
+REF_TOKENS = 4  # reference decode tokens per timed step (a bounded sample of the 128)
+
+
+def ref_tokens_per_step(steps: int, warmup: int) -> int:
+    """Tokens per reference step: REF_TOKENS while the whole run stays inside
+    the workload's positions 64..191, fewer for long runs."""
+    return max(1, min(REF_TOKENS, NEW // max(1, steps + warmup)))
+
+
+def config_for(world: int) -> dict:
+    """The workload both arms report: one independent sequence per GPU."""
+    return dict(CONFIG, global_batch=world,
+                parallelism=f"replicas x{world}" if world > 1 else "single GPU")
 
 
 class Clocks:
@@ -117,12 +138,28 @@ def committed_traffic(name: str):
     return None
 
 
-def reference_sample(threads: int, steps: int, warmup: int, prompt_len=8, n_predict=9):
-    from oracle.binding import run_ref_bench
-    recs = run_ref_bench("qwen2", threads, prompt_len, n_predict, steps, warmup)
+def reference_sample(threads: int, steps: int, warmup: int):
+    """The reference's decode loop on the same seeded model: prompt prefilled
+    once (untimed), then `steps` timed steps of REF_TOKENS greedy tokens
+    continuing the sequence from position PROMPT (oracle/_ref/ref_harness
+    decode).  Returns (tokens/s over the timed steps, their records)."""
+    from oracle.binding import run_ref_decode
+    recs = run_ref_decode("qwen2", threads, PROMPT, ref_tokens_per_step(steps, warmup), steps, warmup)
     timed = [r for r in recs if r.get("event") == "step" and r.get("timed")]
-    vals = [r["decode_tok_s"] for r in timed]
-    return statistics.mean(vals) if vals else None, timed
+    if not timed:
+        return None, timed
+    toks = sum(r["decode_tokens"] for r in timed)
+    ms = sum(r["decode_ms"] for r in timed)
+    return toks * 1000.0 / ms, timed
+
+
+def reference_sample_text(threads: int, steps: int, timed) -> str:
+    n = timed[0]["decode_tokens"] if timed else 0
+    first = timed[0]["first_pos"] if timed else PROMPT
+    last = timed[-1]["first_pos"] + n - 1 if timed else PROMPT
+    return (f"reference RunBenchmark decode loop (src/debug.cpp:112-127) on the same seeded model, "
+            f"{threads} threads: 64-token prompt prefilled once (untimed), {steps} timed steps of "
+            f"{n} greedy tokens at positions {first}..{last}")
 
 
 def max_over_ranks(dist, value: float, device: str) -> float:
@@ -144,10 +181,10 @@ def job_throughput(world: int, tokens_per_rank_step: int, steps: int, secs: floa
 
 def run_reference(args):
     rank = int(os.environ.get("RANK", "0"))
+    world = int(os.environ.get("WORLD_SIZE", "1"))
     if rank != 0:
         return 0
     threads = os.cpu_count() or 1
-    sample = f"reference RunBenchmark on the same model: prompt 8 tokens, 8 decode tokens per step"
     try:
         value, timed = reference_sample(threads, args.steps, args.warmup)
     except Exception as e:  # the harness is built here from the reference tree
@@ -157,13 +194,32 @@ def run_reference(args):
     line = {"metric": METRIC, "value": value, "unit": UNIT, "n_gpus": args.gpus,
             "steps": args.steps, "warmup": args.warmup, "ms_per_step": ms,
             "higher_is_better": True, "scaling": "weak", "vs_baseline": None, "dtype": "f32",
-            "data": "synthetic", "impl": "reference", "config": CONFIG,
+            "data": "synthetic (seeded random-init weights and prompt ids)", "impl": "reference",
+            "config": config_for(world),
             "cpu_baseline": {"value": value, "unit": UNIT, "cores": threads, "kind": "reference",
-                             "sample": sample},
+                             "sample": reference_sample_text(threads, args.steps, timed)},
             "e2e": {"value": value, "unit": UNIT, "h2d_bytes_per_step": 0,
                     "d2h_bytes_per_step": 0}}
     print(json.dumps(line), flush=True)
     return 0
+
+
+def dropin_numbers(timeout: float = 900.0):
+    """The reference's unchanged forward.cpp device path on this library
+    (ForwardBatch over the prompt, then 128 single-token steps with the
+    reference's host arg-max): prompt and decode tokens/s."""
+    exe = os.path.join(ROOT, "oracle", "_ref", "forward_on_b200")
+    if not os.path.exists(exe):
+        return {"value": None, "unit": UNIT, "unavailable": "oracle/_ref/forward_on_b200 not built"}
+    out = subprocess.run([exe, "qwen2", str(PROMPT), str(NEW + 1)], capture_output=True, text=True,
+                         timeout=timeout)
+    if out.returncode != 0:
+        return {"value": None, "unit": UNIT, "unavailable": out.stderr.strip()[-200:]}
+    r = json.loads(out.stdout.strip().splitlines()[-1])
+    return {"value": r["decode_tokens"] * 1000.0 / r["decode_ms"], "unit": UNIT,
+            "prefill_tok_s": PROMPT * 1000.0 / r["prefill_ms"], "decode_tokens": r["decode_tokens"],
+            "path": "reference src/forward.cpp ForwardBatch + GetArgMax over the include/cuda_*.h adapter "
+                    "(one library call per op, logits copied to the host every token)"}
 
 
 def gemv_roofline(lib, dev, torch, stream):
@@ -316,6 +372,25 @@ def run_ours(args):
         gpu_launches = launches_per_token * new * args.steps
     roof["frac"] = roof["achieved"] / roof["peak"]
 
+    # the prompt pass alone: 64 prompt tokens through every layer at once and
+    # the first greedy token, host prompt in, host token out
+    prefill = None
+    if not args.no_prefill:
+        pbuf = torch.from_numpy(np.ascontiguousarray(prompt, np.int32)).pin_memory()
+        one = torch.empty(1, dtype=torch.int32, pin_memory=True)
+        for _ in range(2):
+            lib.call("mlb_session_generate", sess.handle, pbuf.data_ptr(), PROMPT, 0, 1, one.data_ptr())
+        barrier()
+        reps = 10
+        t0 = time.perf_counter()
+        for _ in range(reps):
+            lib.call("mlb_session_generate", sess.handle, pbuf.data_ptr(), PROMPT, 0, 1, one.data_ptr())
+        barrier()
+        psecs = max_over_ranks(dist, (time.perf_counter() - t0) / reps, f"cuda:{dev}")
+        prefill = {"value": world * PROMPT / psecs, "unit": "prompt tokens/s", "ms": psecs * 1e3,
+                   "path": "mlb_session_generate(64-token host prompt -> 1 host token): tensor-core "
+                           "prompt pass + first arg-max"}
+
     sess.close()
     model.close()
     if dist is not None:
@@ -327,19 +402,24 @@ def run_ours(args):
     if world == 1 and not args.no_cpu_baseline:
         threads = os.cpu_count() or 1
         try:
-            v, _ = reference_sample(threads, 1, 1)
+            v, timed = reference_sample(threads, 3, 1)
             cpu = {"value": v, "unit": UNIT, "cores": threads, "kind": "reference",
-                   "sample": "reference RunBenchmark, prompt 8 + 8 decode tokens, 1 timed step"}
+                   "sample": reference_sample_text(threads, 3, timed)}
         except Exception as e:
             cpu = {"value": None, "unit": UNIT, "cores": threads, "kind": "reference",
                    "sample": f"unavailable: {e}"}
+    dropin = None
+    if world == 1 and not args.no_dropin:
+        try:
+            dropin = dropin_numbers()
+        except Exception as e:
+            dropin = {"value": None, "unit": UNIT, "unavailable": str(e)}
     line = {
         "metric": METRIC, "value": value, "unit": UNIT, "n_gpus": world, "steps": args.steps,
         "warmup": args.warmup, "ms_per_step": secs / args.steps * 1e3, "higher_is_better": True,
         "scaling": "weak", "vs_baseline": None, "dtype": "f32 activations, Q8_0 weights",
         "data": "synthetic (seeded random-init weights and prompt ids)",
-        "config": dict(CONFIG, global_batch=world,  # one independent sequence per GPU
-                       parallelism=f"replicas x{world}" if world > 1 else "single GPU"),
+        "config": config_for(world),
         "e2e": {"value": e2e, "unit": UNIT, "h2d_bytes_per_step": 4 + 8 + 4,
                 "d2h_bytes_per_step": NEW * 4 + 4,
                 "path": "mlb_session_generate(host start token -> host 128 token ids)"},
@@ -350,6 +430,8 @@ def run_ours(args):
                           "achieved_gbs": step_gbs,
                           "frac": (step_gbs / peaks["hbm_gbs"]) if step_gbs else None},
         "cpu_baseline": cpu,
+        "prefill": prefill,
+        "dropin": dropin,
         "clocks": clk,
         "gpu_launches": gpu_launches,
     }
@@ -365,6 +447,8 @@ def main():
     ap.add_argument("--impl", default="ours", choices=["ours", "reference"])
     ap.add_argument("--no-cpu-baseline", action="store_true")
     ap.add_argument("--no-e2e", action="store_true")
+    ap.add_argument("--no-dropin", action="store_true",
+                    help="skip the reference forward.cpp on this library (builds the model on the CPU)")
     ap.add_argument("--no-prefill", action="store_true",
                     help="profiling: skip the 64-token prefill (KV cache left empty)")
     ap.add_argument("--graph", action="store_true",

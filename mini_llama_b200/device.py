@@ -84,20 +84,6 @@ class Model:
         a = np.ascontiguousarray(data)
         self.lib.call("mlb_model_set_weight", self.handle, layer, kind, a.ctypes.data, a.nbytes, 1)
 
-    def load_from_oracle(self, om):
-        """Copies every tensor of an oracle model (host) into the device model."""
-        from oracle import binding as ob
-        L = self.spec["n_layers"]
-        kinds_global = [(capi.W_EMBEDDING, ob.T_EMBEDDING), (capi.W_FINAL_NORM, ob.T_FINAL_NORM),
-                        (capi.W_LM_HEAD, ob.T_LM_HEAD)]
-        for k, ok in kinds_global:
-            self.set_weight(-1, k, om.tensor(-1, ok))
-        for l in range(L):
-            for k in range(capi.W_ATTN_NORM, capi.W_DOWN + 1):
-                t = om.tensor(l, k)  # oracle kinds use the same numbering
-                if t is not None:
-                    self.set_weight(l, k, t)
-
     def synthesize(self, seed: int, tied: bool):
         """Generates the synthetic weights on the device: N(0, 0.02) linears
         quantized by the device quantizer, norms = 1, as the oracle does."""

@@ -264,3 +264,32 @@ def run_ref_bench(model: str, threads: int, prompt_len: int, n_predict: int, ste
                           str(n_predict), str(steps), str(warmup)], capture_output=True,
                          text=True, timeout=timeout, check=True)
     return [json.loads(line) for line in out.stdout.splitlines() if line.startswith("{")]
+
+
+def run_ref_decode(model: str, threads: int, prompt_len: int, tokens: int, steps: int, warmup: int,
+                   timeout: float = 900.0):
+    """The reference's decode loop in timed steps (oracle/_ref/ref_harness
+    decode); returns the JSON records."""
+    import json
+    if not os.path.exists(REF_HARNESS):
+        raise RuntimeError(f"reference harness missing: {REF_HARNESS}")
+    out = subprocess.run([REF_HARNESS, "decode", model, str(threads), str(prompt_len), str(tokens),
+                          str(steps), str(warmup)], capture_output=True, text=True, timeout=timeout,
+                         check=True)
+    return [json.loads(line) for line in out.stdout.splitlines() if line.startswith("{")]
+
+
+def load_device_model(model, om) -> None:
+    """Copies every tensor of an oracle model (host) into a device model
+    (mini_llama_b200.device.Model) through mlb_model_set_weight; test and
+    smoke-check input plumbing only."""
+    from mini_llama_b200 import capi
+    globals_ = [(capi.W_EMBEDDING, T_EMBEDDING), (capi.W_FINAL_NORM, T_FINAL_NORM),
+                (capi.W_LM_HEAD, T_LM_HEAD)]
+    for k, ok in globals_:
+        model.set_weight(-1, k, om.tensor(-1, ok))
+    for layer in range(model.spec["n_layers"]):
+        for k in range(capi.W_ATTN_NORM, capi.W_DOWN + 1):
+            t = om.tensor(layer, k)  # oracle kinds use the same numbering
+            if t is not None:
+                model.set_weight(layer, k, t)

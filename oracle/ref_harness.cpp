@@ -8,6 +8,13 @@
 //                                            time the reference RunBenchmark
 //                                            (src/debug.cpp:79-143); one JSON
 //                                            line per step on stdout
+//   ref_harness decode <model> <threads> <prompt_len> <tokens> <steps> <warmup>
+//                                            prefill the prompt once (untimed,
+//                                            ForwardBatch), then time steps of
+//                                            <tokens> greedy decode tokens each,
+//                                            continuing the sequence: the decode
+//                                            loop of RunBenchmark (src/debug.cpp:
+//                                            112-127); one JSON line per step
 //   ref_harness gguf <file> <prompt_len> <n_new> <seed>
 //                                            load a GGUF file (LoadGgufModel)
 //                                            and decode greedily; one JSON line
@@ -32,6 +39,7 @@
 
 #include "include/batch.h"
 #include "include/context.h"
+#include "include/sampler.h"
 #include "include/debug.h"
 #include "include/forward.h"
 #include "include/kv_cache.h"
@@ -329,6 +337,48 @@ int Bench(const std::string& name, int threads, int prompt_len, int n_predict, i
     return 0;
 }
 
+// ---------------------------------------------------------------- decode sample
+// The decode loop of RunBenchmark (src/debug.cpp:112-127) split into timed
+// steps: greedy sampling with seed 0, one single-token batch per position.
+int DecodeSample(const std::string& name, int threads, int prompt_len, int tokens, int steps, int warmup) {
+    ModelSpec s = GetSpec(name);
+    SetThreadCount(threads);
+    auto t0 = std::chrono::steady_clock::now();
+    MiniLlamaModel model = BuildModel(s);
+    std::vector<int> seq = PromptTokens(s, prompt_len);
+    MiniLlamaContext ctx(&model);
+    MiniSampler sampler(0);
+    SamplerParams params;
+    params.seed = 0;
+    auto t1 = std::chrono::steady_clock::now();
+    Tensor logits = ForwardBatch(ctx, model, MiniBatch::GetMultiMiniBatch(seq, 0));
+    seq.push_back(sampler.Sample(logits, params));
+    auto t2 = std::chrono::steady_clock::now();
+    std::printf(
+        "{\"event\": \"built\", \"model\": \"%s\", \"build_s\": %.3f, \"prefill_ms\": %.3f, "
+        "\"threads\": %d}\n",
+        s.name, std::chrono::duration<double>(t1 - t0).count(),
+        std::chrono::duration<double, std::milli>(t2 - t1).count(), GetThreadCount());
+    std::fflush(stdout);
+    for (int i = 0; i < warmup + steps; ++i) {
+        const int first = static_cast<int>(seq.size()) - 1;
+        if (first + tokens > model.config.max_seq_len) throw std::runtime_error("decode sample passes max_seq_len");
+        auto a = std::chrono::steady_clock::now();
+        for (int j = 0; j < tokens; ++j) {
+            logits = ForwardBatch(ctx, model, MiniBatch::GetSingleMiniBatch(seq.back(), static_cast<int>(seq.size()) - 1));
+            seq.push_back(sampler.Sample(logits, params));
+        }
+        auto b = std::chrono::steady_clock::now();
+        const double ms = std::chrono::duration<double, std::milli>(b - a).count();
+        std::printf(
+            "{\"event\": \"step\", \"timed\": %s, \"first_pos\": %d, \"decode_tokens\": %d, "
+            "\"decode_ms\": %.4f, \"decode_tok_s\": %.6f}\n",
+            i >= warmup ? "true" : "false", first, tokens, ms, tokens * 1000.0 / ms);
+        std::fflush(stdout);
+    }
+    return 0;
+}
+
 }  // namespace
 
 int main(int argc, char** argv) {
@@ -359,13 +409,18 @@ int main(int argc, char** argv) {
                         model.config.dim, model.config.head_dim, model.lm_head.type == QuantType::kF32 ? 1 : 0);
             return 0;
         }
+        if (argc == 8 && std::string(argv[1]) == "decode") {
+            return DecodeSample(argv[2], std::atoi(argv[3]), std::atoi(argv[4]), std::atoi(argv[5]),
+                                std::atoi(argv[6]), std::atoi(argv[7]));
+        }
         if (argc == 8 && std::string(argv[1]) == "bench") {
             return Bench(argv[2], std::atoi(argv[3]), std::atoi(argv[4]), std::atoi(argv[5]),
                          std::atoi(argv[6]), std::atoi(argv[7]));
         }
         std::fprintf(stderr,
                      "usage: ref_harness golden <outdir> [case...] | bench <model> <threads> "
-                     "<prompt_len> <n_predict> <steps> <warmup>\n");
+                     "<prompt_len> <n_predict> <steps> <warmup> | decode <model> <threads> <prompt_len> "
+                     "<tokens> <steps> <warmup>\n");
         return 2;
     } catch (const std::exception& e) {
         std::fprintf(stderr, "ref_harness: %s\n", e.what());

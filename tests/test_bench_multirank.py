@@ -88,3 +88,8 @@ def test_reference_arm_line_on_rank_zero():
     if "unavailable" not in line:
         assert line["metric"].startswith("decode tok/s") and line["value"] > 0
         assert line["e2e"]["h2d_bytes_per_step"] == 0
+        # the same workload description as the repo arm's line
+        sys.path.insert(0, ROOT)
+        import bench
+        assert line["config"] == bench.config_for(1)
+        assert "positions 68..71" in line["cpu_baseline"]["sample"]  # after one warm-up step

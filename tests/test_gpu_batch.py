@@ -9,6 +9,7 @@ import pytest
 
 from mini_llama_b200 import capi
 from mini_llama_b200.device import BatchSession, Model, Session
+from oracle.binding import load_device_model
 from oracle.binding import MODEL_SPECS
 
 pytestmark = pytest.mark.gpu
@@ -23,7 +24,7 @@ def prompts(seed, batch, n, vocab):
 def tiny(mlb, gpu, oracle):
     om = oracle.model("tiny")
     m = Model(mlb, gpu, MODEL_SPECS["tiny"])
-    m.load_from_oracle(om)
+    load_device_model(m, om)
     yield om, m
     m.close()
     om.close()

@@ -8,6 +8,7 @@ import pytest
 
 from mini_llama_b200 import capi
 from mini_llama_b200.device import DeviceArray, Model, Session
+from oracle.binding import load_device_model
 from oracle.binding import MODEL_SPECS
 
 pytestmark = pytest.mark.gpu
@@ -24,7 +25,7 @@ def assert_logits(actual, expected, what):
 def oracle_loaded(mlb, gpu, oracle, name):
     om = oracle.model(name)
     m = Model(mlb, gpu, MODEL_SPECS[name])
-    m.load_from_oracle(om)
+    load_device_model(m, om)
     return om, m
 
 

@@ -13,6 +13,7 @@ import pytest
 
 from mini_llama_b200 import capi
 from mini_llama_b200.device import Model, Session
+from oracle.binding import load_device_model
 
 pytestmark = pytest.mark.gpu
 
@@ -37,7 +38,7 @@ def assert_logits(actual, expected, what):
 def variant(request, mlb, gpu, oracle):
     om = oracle.model("tiny", **VARIANTS[request.param])
     m = Model(mlb, gpu, om.spec)
-    m.load_from_oracle(om)
+    load_device_model(m, om)
     yield request.param, om, m
     m.close()
     om.close()
@@ -116,7 +117,7 @@ def test_persistent_rejected_for_unsupported_shapes(mlb, gpu, oracle):
     om = oracle.model("tiny")
     m = Model(mlb, gpu, om.spec)
     try:
-        m.load_from_oracle(om)
+        load_device_model(m, om)
         s = Session(m)
         try:
             assert s.path() == 1
