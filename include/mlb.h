@@ -304,6 +304,18 @@ int mlb_session_use_persistent(mlb_session* session, int enable);
  * (lm_head): 0 wait done, 1 done.  Stamps past `entries` are dropped; the
  * buffer is not cleared.  NULL, 0 turns the timeline off. */
 int mlb_session_trace(mlb_session* session, unsigned long long* device_buffer, size_t entries);
+/* Bound, in nanoseconds, of every wait inside the persistent decode kernel (a
+ * dependency counter, a tagged hand-over word, a weight stage); default 2 s.
+ * A wait that expires makes the call return MLB_ERR_DEVICE_TIMEOUT and leaves
+ * the device usable.  No reference counterpart (the reference has no device
+ * waits). */
+int mlb_session_wait_limit(mlb_session* session, unsigned long long nanoseconds);
+/* Test hook: the persistent kernel withholds every signal of phase counter
+ * `counter` (layer l: 3l + 0 x_mid ready, 3l + 1 attention done, 3l + 2 FFN
+ * done; -1 restores normal operation), so the waits on it expire after the
+ * wait limit.  Exercises the bounded waits and the abort path without any
+ * device fault.  No reference counterpart. */
+int mlb_session_test_withhold_signal(mlb_session* session, int counter);
 /* Device pointers of the session KV cache. */
 int mlb_session_kv_cache(mlb_session* session, float** key_cache, float** value_cache);
 /* Prompts of at least min_tokens tokens (default 16; 0: never) go through

@@ -102,6 +102,8 @@ SIGNATURES = {
     "mlb_session_gemv_path": (_i, [_vp, _pi]),
     "mlb_session_use_persistent": (_i, [_vp, _i]),
     "mlb_session_trace": (_i, [_vp, _vp, _sz]),
+    "mlb_session_wait_limit": (_i, [_vp, ctypes.c_ulonglong]),
+    "mlb_session_test_withhold_signal": (_i, [_vp, _i]),
     "mlb_session_kv_cache": (_i, [_vp, _pp, _pp]),
     "mlb_session_prefill_min": (_i, [_vp, _i]),
     "mlb_nccl_unique_id": (_i, [_vp]),

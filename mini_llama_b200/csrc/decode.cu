@@ -91,6 +91,8 @@ struct mlb_session {
     unsigned long long* qkvt = nullptr;  // tagged q, k, v words (never match a stale tag)
     size_t qkvt_bytes = 0;
     unsigned tag_base = 1;               // next (step 0, layer 0) tag; 0 marks never written
+    unsigned long long wait_ns = 2000000000ull;  // bound of one wait in the persistent kernel
+    int withhold = -1;                   // test hook: a phase counter never signalled
     cudaGraph_t graph = nullptr;
     cudaGraphExec_t exec = nullptr;
     // prompt pass: all prompt tokens through each layer at once (row buffers
@@ -522,6 +524,8 @@ void RunMega(mlb_session* s, DeviceContext& c, int start_pos, int n_steps, int g
         CheckCuda(cudaMemsetAsync(s->qkvt, 0, s->qkvt_bytes, c.stream), "cudaMemsetAsync(qkv words)");
     }
     MegaParams p = s->mp;
+    p.wait_ns = s->wait_ns;
+    p.withhold = s->withhold;
     p.tag_base = s->tag_base;
     s->tag_base += span;
     p.start_pos = start_pos;
@@ -1001,6 +1005,22 @@ int mlb_session_trace(mlb_session* session, unsigned long long* device_buffer, s
         Require(device_buffer != nullptr || entries == 0, "mlb_session_trace", "null buffer");
         session->mp.trace = device_buffer;
         session->mp.trace_cap = device_buffer ? entries : 0;
+    });
+}
+
+int mlb_session_wait_limit(mlb_session* session, unsigned long long nanoseconds) {
+    return Guard([&] {
+        Require(session != nullptr, "mlb_session_wait_limit", "null session");
+        Require(nanoseconds > 0, "mlb_session_wait_limit", "the wait limit must be positive");
+        session->wait_ns = nanoseconds;
+    });
+}
+
+int mlb_session_test_withhold_signal(mlb_session* session, int counter) {
+    return Guard([&] {
+        Require(session != nullptr, "mlb_session_test_withhold_signal", "null session");
+        Require(counter >= -1, "mlb_session_test_withhold_signal", "counter must be -1 or a phase counter");
+        session->withhold = counter;
     });
 }
 

@@ -8,8 +8,7 @@
 namespace mlb {
 namespace {
 
-constexpr int kMkSpin = 1 << 22;                    // poll bound of one dependency wait
-constexpr uint64_t kMkWaitNs = 2000000000ull;       // bound of one shared-memory stage wait
+constexpr int kMkSpin = 1 << 26;  // backstop poll count of one dependency wait (the time bound p.wait_ns comes first)
 
 __device__ __forceinline__ void ConsumerBar() { asm volatile("bar.sync 1, 256;" ::: "memory"); }
 
@@ -134,12 +133,18 @@ __device__ __forceinline__ bool WaitCounter(const MegaParams& p, const MkSmem& s
         bool ok = s.flags[0] == 0;
         if (ok) {
             ok = false;
+            uint64_t t0 = 0;
             for (int it = 0; it < kMkSpin; ++it) {
                 if (LdAcquire(p.counters + ctr) >= target) {
                     ok = true;
                     break;
                 }
-                if ((it & 255) == 255 && LdRelaxedInt(p.status) != 0) break;
+                if ((it & 255) == 255) {
+                    if (LdRelaxedInt(p.status) != 0) break;
+                    const uint64_t now = GlobalTimerNs();
+                    if (t0 == 0) t0 = now;
+                    else if (now - t0 > p.wait_ns) break;
+                }
             }
             if (!ok) atomicCAS(p.status, 0, MLB_ERR_DEVICE_TIMEOUT);
         }
@@ -158,9 +163,11 @@ __device__ __forceinline__ void RedRelease(unsigned* ctr) {
     asm volatile("red.release.gpu.global.add.u32 [%0], 1;" ::"l"(ctr) : "memory");
 }
 
+// (A counter equal to p.withhold is never signalled: the test hook that makes
+// the waits on it expire.)
 __device__ __forceinline__ void Signal(const MegaParams& p, int ctr) {
     ConsumerBar();
-    if (threadIdx.x == 0) RedRelease(p.counters + ctr);
+    if (threadIdx.x == 0 && ctr != p.withhold) RedRelease(p.counters + ctr);
 }
 
 // Waits (every thread) for the stage of chunk rg.n; bounded, and it gives up
@@ -168,7 +175,7 @@ __device__ __forceinline__ void Signal(const MegaParams& p, int ctr) {
 // and sets the sticky abort flag but returns normally: every thread still
 // reaches every barrier, and the CTA leaves at its next phase wait.
 __device__ __forceinline__ void WaitChunk(const MegaParams& p, const MkSmem& s, const Ring& rg) {
-    if (!MbarWaitFor(&s.full[rg.n % kMkStages], (rg.n / kMkStages) & 1, kMkWaitNs, p.status)) {
+    if (!MbarWaitFor(&s.full[rg.n % kMkStages], (rg.n / kMkStages) & 1, p.wait_ns, p.status)) {
         atomicCAS(p.status, 0, MLB_ERR_DEVICE_TIMEOUT);
         s.flags[0] = 1;
     }
@@ -825,13 +832,19 @@ __device__ unsigned Consumers(const MegaParams& p, const MkSmem& s) {
                                                  : size_t(p.qd) + (part - 1) * p.kd + size_t(kvh) * hd + d;
                     unsigned long long wv = 0;
                     bool got = false;
+                    uint64_t t0 = 0;
                     for (int it2 = 0; it2 < kMkSpin; ++it2) {
                         wv = LdTagged(p.qkvt + src);
                         if (static_cast<unsigned>(wv >> 32) == tag) {
                             got = true;
                             break;
                         }
-                        if ((it2 & 255) == 255 && LdRelaxedInt(p.status) != 0) break;
+                        if ((it2 & 255) == 255) {
+                            if (LdRelaxedInt(p.status) != 0) break;
+                            const uint64_t now = GlobalTimerNs();
+                            if (t0 == 0) t0 = now;
+                            else if (now - t0 > p.wait_ns) break;
+                        }
                     }
                     if (!got) {
                         atomicCAS(p.status, 0, MLB_ERR_DEVICE_TIMEOUT);
@@ -1192,7 +1205,7 @@ __global__ void __launch_bounds__(kMkThreads, 1) MegaDecodeKernel(const MegaPara
     if (threadIdx.x == 0) {
         const unsigned issued = static_cast<unsigned>(s.flags[5]);
         for (unsigned k = issued > kMkStages ? issued - kMkStages : 0; k < issued; ++k)
-            MbarWaitFor(&s.full[k % kMkStages], (k / kMkStages) & 1, kMkWaitNs, nullptr);
+            MbarWaitFor(&s.full[k % kMkStages], (k / kMkStages) & 1, p.wait_ns, nullptr);
     }
 }
 

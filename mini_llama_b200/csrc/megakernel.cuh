@@ -85,6 +85,8 @@ struct MegaParams {
     int gen_from;  // hist[pos + 1] is written only when pos + 1 >= gen_from
     int* next_token;
     int* status;
+    unsigned long long wait_ns;  // bound of one wait (dependency counter, tagged word, weight stage)
+    int withhold;                // test hook: this counter is never signalled (-1: none)
     int stage_bytes;
     int list_cap;  // capacity of the per-CTA chunk list (MegaListCap)
     int kst_rows;  // cached K rows an attention item stages in shared memory (0..kMkAttnChunk)

@@ -129,3 +129,35 @@ def test_persistent_rejected_for_unsupported_shapes(mlb, gpu, oracle):
     finally:
         m.close()
         om.close()
+
+
+def test_bounded_wait_expires_and_device_recovers(mlb, gpu, variant):
+    """A phase signal withheld by the host: every wait on it gives up after the
+    session's wait limit, the call returns MLB_ERR_DEVICE_TIMEOUT (no fault,
+    trap or hang: the waiting CTAs record the status and leave, the others
+    see it and leave too), and the same session then decodes the oracle's
+    tokens."""
+    import time
+    name, om, m = variant
+    prompt = om.prompt(6)
+    n_new = 12
+    gen_ref, _ = om.greedy(prompt, n_new)
+    s = Session(m)
+    try:
+        s.use_persistent(True)
+        mlb.call("mlb_session_wait_limit", s.handle, 2_000_000)  # 2 ms
+        mlb.call("mlb_session_test_withhold_signal", s.handle, 2)  # layer 0's FFN done
+        p = np.asarray(prompt, np.int32)
+        out = np.zeros(n_new, np.int32)
+        t0 = time.perf_counter()
+        st = mlb.raw("mlb_session_generate", s.handle, p.ctypes.data, len(p), 0, n_new, out.ctypes.data)
+        elapsed = time.perf_counter() - t0
+        assert st == capi.MLB_ERR_DEVICE_TIMEOUT, (name, st, mlb.last_error())
+        assert "bounded device wait expired" in mlb.last_error()
+        assert elapsed < 10.0, f"{name}: the expired wait took {elapsed:.1f} s to return"
+        mlb.call("mlb_session_test_withhold_signal", s.handle, -1)
+        mlb.call("mlb_session_wait_limit", s.handle, 2_000_000_000)
+        s.reset()
+        assert list(s.generate(prompt, n_new)) == list(gen_ref), f"{name}: tokens after the expired wait"
+    finally:
+        s.close()
