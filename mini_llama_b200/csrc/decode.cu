@@ -79,6 +79,7 @@ struct mlb_session {
     int* state = nullptr;  // [0] pos, [1] gen_from, [2] next token, [3] status
     int* hist = nullptr;   // [max_seq_len + 1]
     int chunks = 1;
+    bool merge_in_oproj = true;  // the O-projection's prologue merges the attention partials
     size_t cache_floats = 0;
     // persistent decode kernel
     bool mega_ok = false;  // the model's shapes fit it
@@ -225,8 +226,11 @@ void PrepareR16(mlb_model* m, DeviceContext& c, int chunks) {
         return QmmaSmem::Bytes(1, nb, tiles_per_stage * nb * kR16Chunk, 2, aux);
     };
     const mlb_model_config& cf = m->cfg;
+    // (the O-projection's merge prologue is optional: when the attention
+    // partials do not fit it, the step merges them in a separate kernel)
+    (void)chunks;
     const size_t worst = std::max({need(cf.dim, 2, cf.dim), need(cf.hidden_dim, 1, 0),
-                                   need(cf.n_heads * cf.head_dim, 1, cf.n_heads * chunks * (cf.head_dim + 2))});
+                                   need(cf.n_heads * cf.head_dim, 1, 0)});
     if (worst + 4096 > static_cast<size_t>(c.max_smem_optin)) return;
     size_t off = 0;
     auto slot = [&](int kind) {
@@ -287,6 +291,22 @@ void CaptureStep(mlb_session* s, DeviceContext& c) {
     auto WL = [&](int l, int kind) {
         return r16 ? m->R16(l, kind) : static_cast<const uint8_t*>(m->Ptr(m->Get(l, kind)));
     };
+    // The O-projection merges the step's attention partials in its prologue
+    // when they fit its shared memory, else a merge kernel runs first.
+    if (s->chunks > 1) {
+        GemvParams p = {};
+        p.K = qd;
+        p.nseg = 1;
+        p.seg[0] = GemvSeg{WL(0, MLB_W_WO), nullptr, cf.dim, 0, 0, 0};
+        p.part_ml = s->part_ml;
+        p.part_o = s->part_o;
+        p.n_heads = cf.n_heads;
+        p.head_dim = cf.head_dim;
+        p.chunks = s->chunks;
+        const GemvPlan plan = r16 ? PlanQmma(p, 1, false, c.sm_count, c.max_smem_optin, 1, kRingBudget)
+                                  : PlanGemv(p, qt, 1, false, c.sm_count, c.max_smem_optin, 1, kRingBudget);
+        s->merge_in_oproj = plan.ok;
+    }
 
     CheckCuda(cudaStreamBeginCapture(st, cudaStreamCaptureModeThreadLocal), "cudaStreamBeginCapture");
     try {
@@ -353,14 +373,21 @@ void CaptureStep(mlb_session* s, DeviceContext& c) {
                 p.y_stride = cf.dim;
                 p.residual = s->x;
                 p.res_stride = cf.dim;
-                p.part_ml = s->part_ml;
-                p.part_o = s->part_o;
-                p.n_heads = cf.n_heads;
-                p.head_dim = cf.head_dim;
-                p.chunks = s->chunks;
                 p.status = status;
-                gemv(p, false, s->chunks > 1 ? kProAttnMerge : kProPlain, kEpiResidual,
-                     "O-projection");
+                if (s->chunks > 1 && s->merge_in_oproj) {
+                    p.part_ml = s->part_ml;
+                    p.part_o = s->part_o;
+                    p.n_heads = cf.n_heads;
+                    p.head_dim = cf.head_dim;
+                    p.chunks = s->chunks;
+                    gemv(p, false, kProAttnMerge, kEpiResidual, "O-projection");
+                } else {
+                    // long caches: more partials than the prologue holds; the
+                    // merge kernel writes the attention rows first
+                    if (s->chunks > 1)
+                        LaunchAttnMerge(s->part_ml, s->part_o, s->chunks, cf.head_dim, s->attn, cf.n_heads, st);
+                    gemv(p, false, kProPlain, kEpiResidual, "O-projection");
+                }
             }
             // 4. RMSNorm + gate/up + SwiGLU
             {
