@@ -10,7 +10,8 @@ sequences.  Q, K, V ~ N(0, 1) from the seeded device generator (seed 4).  The
 cache is the reference layout [batch][n_layers = 1][P][n_kv][head_dim] fp32.
 Batch 1 runs mlb_attention_decode, batch 32 mlb_attention_decode_batched
 (every sequence at the same position), each timed with CUDA events on the
-library stream after warm-up, the L2 flushed (a 256 MB write) before every
+library stream after warm-up, the L2 flushed (a 256 MB write, then a read of
+it, leaving clean lines) before every
 launch and all reps queued before the first is waited for, and printed as one
 JSON line per case:
   bytes   algorithmic bytes: K and V rows read (2 x P x n_kv x head_dim x 4
@@ -50,6 +51,7 @@ def time_case(lib, dev, torch, stream, nh, nkv, hd, ctx, batch, reps=10):
         host = np.full(batch, pos, dtype=np.int32)
         lib.call("mlb_memcpy_h2d", dev, positions, host.ctypes.data, host.nbytes)
     flush = lib.malloc(dev, 256 << 20)
+    idx = lib.malloc(dev, 16)
 
     def run():
         if batch == 1:
@@ -63,7 +65,9 @@ def time_case(lib, dev, torch, stream, nh, nkv, hd, ctx, batch, reps=10):
     lib.call("mlb_synchronize", dev)
     events = []
     for _ in range(reps):
+        # flush: a 256 MB write, then a read of it (the L2 keeps clean lines)
         lib.call("mlb_memset", dev, flush, 1, 256 << 20)
+        lib.call("mlb_argmax", dev, flush, (256 << 20) // 4, idx)
         e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
         e0.record(stream)
         run()
@@ -71,7 +75,7 @@ def time_case(lib, dev, torch, stream, nh, nkv, hd, ctx, batch, reps=10):
         events.append((e0, e1))
     lib.call("mlb_synchronize", dev)
     secs = sum(e0.elapsed_time(e1) for e0, e1 in events) / 1e3 / reps
-    for p in (kc, vc, q, out, flush) + ((positions,) if positions else ()):
+    for p in (kc, vc, q, out, flush, idx) + ((positions,) if positions else ()):
         lib.free(dev, p)
     algo = batch * (2 * ctx * nkv * hd * 4 + 2 * nh * hd * 4)
     return secs, algo

@@ -1,7 +1,9 @@
 // Quantized linear entry points (replace mini_llama include/cuda_quant.h:13-38
 // and the kernels of src/cuda_quant.cu:40-135).
+#include <algorithm>
 #include <numeric>
 
+#include "blockmma.cuh"
 #include "qgemv.cuh"
 
 namespace mlb {
@@ -52,6 +54,95 @@ GemvPlan PlanGemv(GemvParams& p, int qtype, int M, bool dual, int sm_count, int 
     plan.grid = std::max(1, std::min(total, sm_count * ctas_per_sm));
     plan.ok = true;
     return plan;
+}
+
+BmPlan PlanBlockMma(BmParams& p, int qtype, int M, int sm_count, int max_smem) {
+    BmPlan plan;
+    const int bb = BlockBytes(qtype);
+    p.nb = (p.K + 31) / 32;
+    p.rowbytes = p.nb * bb;
+    p.tiles = (p.N + 15) / 16;
+    if (reinterpret_cast<uintptr_t>(p.w) & 15) return plan;
+    // Q8_0 / Q4_0 blocks are read in pairs
+    if (qtype != MLB_Q4_1 && (p.nb & 1)) return plan;
+    // below about 1.5 row tiles per SM the weights are too few to stream
+    // (each pair would run its tile's pieces one after another): the other
+    // GEMV splits K across warps instead
+    if (2 * p.tiles < 3 * sm_count) return plan;
+    constexpr int kMaxStage = 20 * 1024;
+    const long long tile_bytes = 16LL * p.rowbytes;
+    if (tile_bytes <= kMaxStage) {
+        p.kc = p.nb;
+        p.units_k = 1;
+        p.pitch = p.rowbytes;  // 16 contiguous GGUF rows
+        p.stage_bytes = static_cast<int>((tile_bytes + 15) & ~15LL);
+    } else if (p.rowbytes % 16 == 0) {
+        // pieces of kc blocks (a multiple of 8) start and end 16-byte aligned;
+        // rows land at a pitch of 16 mod 32 bytes (4 mod 8 words)
+        p.kc = std::min(p.nb, std::max(8, kMaxStage / (16 * bb) / 8 * 8));
+        p.units_k = (p.nb + p.kc - 1) / p.kc;
+        p.pitch = p.kc * bb;
+        if (p.pitch % 32 == 0) p.pitch += 16;
+        p.stage_bytes = 16 * p.pitch;
+    } else {
+        return plan;
+    }
+    p.rowmap = ((p.pitch / 4) % 4 == 2) ? 1 : 0;
+    p.slots = 2;
+    constexpr int kMaxPairs = kBmMaxWarps / 2;
+    const size_t budget = static_cast<size_t>(max_smem) - 1024;
+    plan.grid = sm_count;
+    // as many pairs as fit (the tile scheduler balances them), at most one per
+    // tile of an SM's share
+    int pairs = std::min(kMaxPairs, (p.tiles + plan.grid - 1) / plan.grid);
+    while (pairs > 0 && BmSmem::Bytes(M, p.nb, pairs, p.slots, p.stage_bytes, qtype == MLB_Q4_1) > budget) --pairs;
+    // x's tables span all of K: when they leave room for fewer than three
+    // pairs (long rows, many rows of x), too few copies are in flight
+    if (pairs < std::min(3, (p.tiles + plan.grid - 1) / plan.grid)) return plan;
+    plan.warps = 2 * pairs;
+    plan.smem = BmSmem::Bytes(M, p.nb, pairs, p.slots, p.stage_bytes, qtype == MLB_Q4_1);
+    plan.ok = plan.smem <= budget;
+    return plan;
+}
+
+template <int QT, int M>
+void LaunchBlockMmaT(const BmParams& p, const BmPlan& plan, cudaStream_t stream) {
+    auto kernel = BlockMmaGemvKernel<QT, M>;
+    static int configured_smem[64] = {};  // per instantiation and device
+    int dev = 0;
+    CheckCuda(cudaGetDevice(&dev), "cudaGetDevice");
+    if (dev >= 64 || configured_smem[dev] < static_cast<int>(plan.smem)) {
+        CheckCuda(cudaFuncSetAttribute(kernel, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                                       static_cast<int>(plan.smem)),
+                  "cudaFuncSetAttribute(BlockMmaGemvKernel)");
+        if (dev < 64) configured_smem[dev] = static_cast<int>(plan.smem);
+    }
+    Launch("BlockMmaGemvKernel", kernel, dim3(plan.grid), dim3(32 * plan.warps), plan.smem, stream,
+           false, p);
+}
+
+template <int QT>
+void LaunchBlockMmaM(int M, const BmParams& p, const BmPlan& plan, cudaStream_t stream) {
+    switch (M) {
+        case 1: return LaunchBlockMmaT<QT, 1>(p, plan, stream);
+        case 2: return LaunchBlockMmaT<QT, 2>(p, plan, stream);
+        case 3: return LaunchBlockMmaT<QT, 3>(p, plan, stream);
+        case 4: return LaunchBlockMmaT<QT, 4>(p, plan, stream);
+        case 5: return LaunchBlockMmaT<QT, 5>(p, plan, stream);
+        case 6: return LaunchBlockMmaT<QT, 6>(p, plan, stream);
+        case 7: return LaunchBlockMmaT<QT, 7>(p, plan, stream);
+        case 8: return LaunchBlockMmaT<QT, 8>(p, plan, stream);
+    }
+    Fail(MLB_ERR_UNSUPPORTED, "block-MMA GEMV: unsupported row count");
+}
+
+void LaunchBlockMma(int qtype, int M, const BmParams& p, const BmPlan& plan, cudaStream_t stream) {
+    switch (qtype) {
+        case MLB_Q8_0: return LaunchBlockMmaM<MLB_Q8_0>(M, p, plan, stream);
+        case MLB_Q4_0: return LaunchBlockMmaM<MLB_Q4_0>(M, p, plan, stream);
+        case MLB_Q4_1: return LaunchBlockMmaM<MLB_Q4_1>(M, p, plan, stream);
+    }
+    Fail(MLB_ERR_UNSUPPORTED, "block-MMA GEMV: unsupported block type");
 }
 
 template <int QT, int M, int PRO, int EPI>
@@ -156,6 +247,23 @@ void LinearRows(DeviceContext& c, int qtype, const float* x, const uint8_t* wb, 
 
     for (int m0 = 0; m0 < rows;) {
         int M = std::min(rows - m0, kGemvMaxM);
+        {
+            // tensor-core GEMV over the blocks, when the shape suits it
+            BmParams bp = {};
+            bp.w = wb;
+            bp.K = in_features;
+            bp.N = out_features;
+            const BmPlan bplan = PlanBlockMma(bp, qtype, M, c.sm_count, c.max_smem_optin);
+            if (bplan.ok) {
+                bp.x = x + static_cast<size_t>(m0) * in_features;
+                bp.y = y + static_cast<size_t>(m0) * out_features;
+                bp.bias = bias;
+                bp.status = c.status;
+                LaunchBlockMma(qtype, M, bp, bplan, c.stream);
+                m0 += M;
+                continue;
+            }
+        }
         GemvParams p = {};
         p.K = in_features;
         p.nseg = 1;

@@ -7,9 +7,10 @@ device to each block type; x ~ N(0, 1); shapes [N, K] = [896, 896],
 [4864, 896], [896, 4864], [151936, 896]; M rows of x.  Each case is timed
 through the public entry point (mlb_quant_linear: M <= 8 runs the GEMV, M >= 9
 the tcgen05 kernel, including its x pre-pass) with CUDA events on the
-library stream, after warm-up, with the L2 flushed (a 256 MB write) before
-every launch and all reps queued before the first is waited for (device time,
-not host launch latency), and printed as one JSON line:
+library stream, after warm-up, with the L2 flushed before every launch (a
+256 MB write, then a read of the same buffer, which leaves clean lines) and
+all reps queued before the first is waited for (device time, not host launch
+latency), and printed as one JSON line:
   gbs     algorithmic bytes (W blocks + 4 M K + 4 M N) / time, against the
           measured HBM copy bandwidth (MEASURED_PEAKS.json) -- the bound for
           M <= 8
@@ -55,6 +56,7 @@ def time_case(lib, dev, torch, stream, qtype, n, k, m, reps=10):
     lib.call("mlb_synth_normal", dev, xs, m * k, 2, 9, 1.0)
     y = DeviceArray(lib, dev, (m, n))
     flush = lib.malloc(dev, 256 << 20)
+    idx = lib.malloc(dev, 16)
 
     def run():
         lib.call("mlb_quant_linear", dev, qtype, xs, w, n * nb, m, k, n, None, y.ptr)
@@ -67,7 +69,11 @@ def time_case(lib, dev, torch, stream, qtype, n, k, m, reps=10):
     # device time only, not host launch latency
     events = []
     for _ in range(reps):
+        # flush: a 256 MB write, then a read of it, so the L2 holds clean lines
+        # of the flush buffer (no write-back of dirty lines lands in the timed
+        # call)
         lib.call("mlb_memset", dev, flush, 1, 256 << 20)
+        lib.call("mlb_argmax", dev, flush, (256 << 20) // 4, idx)
         e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
         e0.record(stream)
         run()
@@ -75,7 +81,7 @@ def time_case(lib, dev, torch, stream, qtype, n, k, m, reps=10):
         events.append((e0, e1))
     lib.call("mlb_synchronize", dev)
     total = sum(e0.elapsed_time(e1) for e0, e1 in events) / 1e3
-    for p in (w, xs, flush):
+    for p in (w, xs, flush, idx):
         lib.free(dev, p)
     secs = total / reps
     algo = wbytes + 4 * m * k + 4 * m * n

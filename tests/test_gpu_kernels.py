@@ -132,6 +132,45 @@ def test_linear_microbench_shapes(mlb, gpu, oracle, qtype, n, k, m):
                         linear_terms(x, bench_dequant(oracle, qtype, n, k)), f"{QNAME[qtype]} [{n},{k}] M={m}")
 
 
+# Shapes of more than 1.5 16-row tiles per SM, which take the tensor-core
+# GEMV over the blocks for 1..8 rows where x's tables fit, covering its unit
+# and bank layouts: K = 4864 (rows split into 8-block pieces copied row by
+# row; 3 and 8 rows of x take the other GEMV), 1024 (16 whole rows per copy,
+# row pitch 0 mod 8 words), 576 (odd pitch in words), 896 (pitch 2 mod 4
+# words: interleaved rows), 800 (odd block count: Q4_1 here, the other GEMV
+# for Q8_0 / Q4_0); N = 4099 ends on a partial tile.
+BLOCK_MMA_SHAPES = [(4099, 4864), (4099, 1024), (4099, 576), (4099, 896), (4099, 800)]
+
+
+@pytest.mark.parametrize("qtype", [Q80, Q40, Q41])
+@pytest.mark.parametrize("n,k", BLOCK_MMA_SHAPES)
+def test_linear_block_mma_layouts(mlb, gpu, oracle, qtype, n, k):
+    w = oracle.normal(n * k, 2, STREAM_W + 3000 + k, 0.02).reshape(n, k)
+    blocks = oracle.quantize(qtype, w)
+    wdq = oracle.dequantize(qtype, blocks, n, k)
+    bias = oracle.normal(n, 2, 3001, 0.1)
+    for m in (1, 3, 8):
+        x = oracle.normal(m * k, 2, STREAM_X + 3000 + k + m, 1.0).reshape(m, k)
+        expect = oracle.linear(qtype, x, blocks, n)
+        assert_linear_close(linear_gpu(mlb, gpu, qtype, x, blocks, n), expect, linear_terms(x, wdq),
+                            f"{QNAME[qtype]} [{n},{k}] M={m}")
+        assert_linear_close(linear_gpu(mlb, gpu, qtype, x, blocks, n, bias), expect + bias,
+                            linear_terms(x, wdq, bias), f"{QNAME[qtype]} [{n},{k}] M={m} bias")
+
+
+def test_linear_block_mma_repeated_calls(mlb, gpu, oracle):
+    """The GEMV's tile scheduler resets itself at the end of every launch:
+    calls in a row, of different shapes, each give the full result."""
+    cases = [(151936 // 8, 896, 1), (4099, 4864, 1), (4864, 896, 5)]
+    for rep in range(2):
+        for (n, k, m) in cases:
+            blocks = bench_blocks(oracle, Q80, n, k)
+            x = oracle.normal(m * k, 2, STREAM_X + 4000 + n + m + rep, 1.0).reshape(m, k)
+            got = linear_gpu(mlb, gpu, Q80, x, blocks, n)
+            assert_linear_close(got, oracle.linear(Q80, x, blocks, n),
+                                linear_terms(x, bench_dequant(oracle, Q80, n, k)), f"[{n},{k}] M={m} call {rep}")
+
+
 def test_linear_misaligned_weight_pointer(mlb, gpu, oracle):
     """A weight pointer off the 16-byte grid takes the direct-load kernel."""
     n, k = 33, 96
