@@ -8,7 +8,8 @@
 // pair of warps owns whole row tiles (all their units in turn) and its own
 // ring of shared-memory slots; the leader moves a whole-row unit with one bulk
 // copy (16 GGUF rows are contiguous), a split unit with one bulk copy per row
-// (lanes 0..15), completing on the slot's mbarrier.  The two warps split each
+// (lanes 0..15), completing on the slot's mbarrier; weights are read once, so
+// the copies mark their lines first to leave the L2.  The two warps split each
 // unit's blocks in halves and meet at one named barrier per unit (after which
 // the slot is refilled), adding the follower's partial sums at the end of a
 // tile.  Each pair starts on two fixed tiles and then takes the next free tile
@@ -92,9 +93,9 @@ struct BmTraits<MLB_Q4_1> {
 };
 
 // Shared memory: slots [pairs][slots][stage_bytes] | mbarriers [pairs][slots]
-// | slot tile numbers [pairs][slots] int | x rows [M][kpad] floats (after the
-// prologue: per pair the follower's partial sums [2][NJ][2][32] float2 and the
-// tile's column sums [16][8 NJ] floats) | B fragments [nb][NJ][32] uint2 |
+// | slot tile numbers [pairs][slots] int | per pair the follower's partial
+// sums [2][NJ][2][32] float2 (the buffer just read then holds the tile's
+// column sums [16][8 NJ] floats) | B fragments [nb][NJ][32] uint2 |
 // column records [nb][NJ][4] float4 | Q4_1: x block sums [nb][NJ][4] float2.
 struct BmSmem {
     static __host__ __device__ size_t Ring(int pairs, int slots, int stage_bytes) {
@@ -103,19 +104,17 @@ struct BmSmem {
     static __host__ __device__ size_t Bars(int pairs, int slots) {
         return (size_t(pairs) * slots * 12 + 15) & ~size_t(15);
     }
-    static __host__ __device__ size_t PairScratch(int M) { return size_t(BmMmas(M)) * (2 * 2 * 32 * 8 + 16 * 8 * 4); }
-    static __host__ __device__ size_t X(int M, int nb, int pairs) {
-        const size_t xrows = size_t(M) * nb * 32 * 4;
-        const size_t scratch = size_t(pairs) * PairScratch(M);
-        return xrows > scratch ? xrows : scratch;
-    }
+    // two buffers (tile parity) of [NJ][2][32] float2; the leader turns the
+    // one it has read into the tile's column sums [16][8 NJ] floats
+    static __host__ __device__ size_t PairScratch(int M) { return size_t(BmMmas(M)) * 2 * 2 * 32 * 8; }
+    static __host__ __device__ size_t Scratch(int M, int pairs) { return size_t(pairs) * PairScratch(M); }
     static __host__ __device__ size_t Frag(int M, int nb) { return size_t(nb) * BmMmas(M) * 256; }
     // records (float4), then for Q4_1 the x block sums (float2)
     static __host__ __device__ size_t Rec(int M, int nb, bool sums) {
         return size_t(nb) * BmMmas(M) * (sums ? 64 + 32 : 64);
     }
     static __host__ __device__ size_t Bytes(int M, int nb, int pairs, int slots, int stage_bytes, bool sums) {
-        return Ring(pairs, slots, stage_bytes) + Bars(pairs, slots) + X(M, nb, pairs) + Frag(M, nb) +
+        return Ring(pairs, slots, stage_bytes) + Bars(pairs, slots) + Scratch(M, pairs) + Frag(M, nb) +
                Rec(M, nb, sums);
     }
 };
@@ -275,86 +274,105 @@ __device__ __forceinline__ bool PairBarrierOr(int id, bool flag) {
     return r != 0;
 }
 
-// x rows -> digit-plane B fragments and column records (all warps; ends with a
-// CTA barrier).  xs holds M rows of kpad floats, zero padded past K.
+// x rows -> digit-plane B fragments and column records (all threads; ends
+// with a CTA barrier).  Eight threads per (x row m, block b), one 4-element
+// group each, for m < kRows: a row past M fills the spare columns with zero
+// digits and weights.  x is read from global memory (rows of K floats).
 template <int QT, int M>
-__device__ __forceinline__ void BmBuildTables(const float* xs, int nb, uint2* frags, float4* recs,
+__device__ __forceinline__ void BmBuildTables(const float* x, int K, int nb, uint2* frags, float4* recs,
                                               float2* xsums) {
     constexpr int NJ = BmMmas(M);
     constexpr int kCols = 8 * NJ;
     constexpr int kRows = (kCols + 2) / 3;  // x rows whose columns fill the MMAs
-    const int lane = threadIdx.x & 31;
-    const int kpad = nb * 32;
-    // One thread per (x row m, block b) for m < kRows: a row past M fills the
-    // spare columns with zero digits and weights (and, for Q4_0, the
-    // accumulator start 1.5*2^23: a zero start would read a negative sum as a
-    // NaN pattern).  A thread reads its block's eight 4-element groups
-    // starting at group lane % 8, so the threads of a warp hit different banks.
-    for (int item = threadIdx.x; item < kRows * nb; item += blockDim.x) {
-        const int m = item / nb, b = item - m * nb;
-        const float4* xb = reinterpret_cast<const float4*>(xs + m * kpad + b * 32);
-        float4 f[8];
+    const int sub = threadIdx.x & 7;        // group: elements 4 sub .. 4 sub + 3
+    const int total = kRows * nb;
+    const int per_round = blockDim.x >> 3;
+    // the same number of rounds for every thread, so the group shuffles
+    // always see the whole warp
+    for (int base = 0; base < total; base += per_round) {
+        const int item = base + (threadIdx.x >> 3);
+        const bool live = item < total;
+        const int m = live ? item / nb : 0, b = live ? item - m * nb : 0;
+        float v[4] = {0.0f, 0.0f, 0.0f, 0.0f};
+        if (live && m < M) {
+            const int k0 = b * 32 + 4 * sub;
+            const float* src = x + size_t(m) * K + k0;
+            if (k0 + 4 <= K && (reinterpret_cast<uintptr_t>(src) & 15) == 0) {
+                const float4 f = __ldg(reinterpret_cast<const float4*>(src));
+                v[0] = f.x;
+                v[1] = f.y;
+                v[2] = f.z;
+                v[3] = f.w;
+            } else {
 #pragma unroll
-        for (int q = 0; q < 8; ++q) f[q] = m < M ? xb[(q + lane) & 7] : make_float4(0.0f, 0.0f, 0.0f, 0.0f);
-        float mx = 0.0f;
+                for (int i = 0; i < 4; ++i) v[i] = k0 + i < K ? __ldg(src + i) : 0.0f;
+            }
+        }
+        float mx = fmaxf(fmaxf(fabsf(v[0]), fabsf(v[1])), fmaxf(fabsf(v[2]), fabsf(v[3])));
 #pragma unroll
-        for (int q = 0; q < 8; ++q)
-            mx = fmaxf(mx, fmaxf(fmaxf(fabsf(f[q].x), fabsf(f[q].y)), fmaxf(fabsf(f[q].z), fabsf(f[q].w))));
+        for (int o = 1; o < 8; o <<= 1) mx = fmaxf(mx, __shfl_xor_sync(0xffffffffu, mx, o));
         const int e = static_cast<int>((__float_as_uint(mx) >> 23) & 0xff) - 126;  // mx < 2^e
         float up = 0.0f, s = 0.0f;
         if (mx > 0.0f && e >= -104) {
             up = __uint_as_float(static_cast<uint32_t>(127 + 22 - e) << 23);
             s = __uint_as_float(static_cast<uint32_t>(127 + e - 22) << 23);
         }
+        uint32_t wd[3] = {0u, 0u, 0u};  // planes 2^16, 2^8, 1
         int dsum[3] = {0, 0, 0};
-        float xsum = 0.0f;
+        float xsum = (v[0] + v[1]) + (v[2] + v[3]);
 #pragma unroll
-        for (int q = 0; q < 8; ++q) {
-            const int qq = (q + lane) & 7;  // elements 4qq .. 4qq + 3
-            const float vals[4] = {f[q].x, f[q].y, f[q].z, f[q].w};
-            uint32_t wd[3] = {0u, 0u, 0u};  // planes 2^16, 2^8, 1
+        for (int i = 0; i < 4; ++i) {
+            const int xi = __float2int_rn(v[i] * up);
+            const int d0 = (xi << 24) >> 24;
+            const int x1 = (xi - d0) >> 8;
+            const int d1 = (x1 << 24) >> 24;
+            const int d2 = (x1 - d1) >> 8;
+            wd[0] |= (static_cast<uint32_t>(d2) & 0xffu) << (8 * i);
+            wd[1] |= (static_cast<uint32_t>(d1) & 0xffu) << (8 * i);
+            wd[2] |= (static_cast<uint32_t>(d0) & 0xffu) << (8 * i);
+            dsum[0] += d2;
+            dsum[1] += d1;
+            dsum[2] += d0;
+        }
+        if constexpr (QT == MLB_Q4_0) {
 #pragma unroll
-            for (int i = 0; i < 4; ++i) {
-                const int x = __float2int_rn(vals[i] * up);
-                const int d0 = (x << 24) >> 24;
-                const int x1 = (x - d0) >> 8;
-                const int d1 = (x1 << 24) >> 24;
-                const int d2 = (x1 - d1) >> 8;
-                wd[0] |= (static_cast<uint32_t>(d2) & 0xffu) << (8 * i);
-                wd[1] |= (static_cast<uint32_t>(d1) & 0xffu) << (8 * i);
-                wd[2] |= (static_cast<uint32_t>(d0) & 0xffu) << (8 * i);
-                dsum[0] += d2;
-                dsum[1] += d1;
-                dsum[2] += d0;
-                xsum += vals[i];
-            }
-            // column c of MMA c / 8 is fragment lane 4 (c % 8) + (k & 15) / 4,
-            // word k / 16
+            for (int o = 1; o < 8; o <<= 1)
 #pragma unroll
-            for (int pl = 0; pl < 3; ++pl) {
-                const int c = 3 * m + pl;
-                if (c < kCols) {
-                    uint32_t* fw = reinterpret_cast<uint32_t*>(frags + (size_t(b) * NJ + (c >> 3)) * 32);
-                    fw[(4 * (c & 7) + (qq & 3)) * 2 + (qq >> 2)] = wd[pl];
-                }
+                for (int pl = 0; pl < 3; ++pl) dsum[pl] += __shfl_xor_sync(0xffffffffu, dsum[pl], o);
+        }
+        if constexpr (QT == MLB_Q4_1) {
+#pragma unroll
+            for (int o = 1; o < 8; o <<= 1) xsum += __shfl_xor_sync(0xffffffffu, xsum, o);
+        }
+        if (!live) continue;
+        // column c of MMA c / 8 is fragment lane 4 (c % 8) + (k & 15) / 4,
+        // word k / 16; this thread's elements k = 4 sub + i
+#pragma unroll
+        for (int pl = 0; pl < 3; ++pl) {
+            const int c = 3 * m + pl;
+            if (c < kCols) {
+                uint32_t* fw = reinterpret_cast<uint32_t*>(frags + (size_t(b) * NJ + (c >> 3)) * 32);
+                fw[(4 * (c & 7) + (sub & 3)) * 2 + (sub >> 2)] = wd[pl];
             }
         }
         // records: lane t of MMA j reads record (b, j, t) = w of columns
         // 8j + 2t (x) and 8j + 2t + 1 (y), then -(1.5*2^23 + c) w of the same
         // two columns (all exact: w is a power of two or 0)
-        const float pw[3] = {65536.0f, 256.0f, 1.0f};
+        if (sub == 0) {
+            const float pw[3] = {65536.0f, 256.0f, 1.0f};
 #pragma unroll
-        for (int pl = 0; pl < 3; ++pl) {
-            const int c = 3 * m + pl;
-            if (c >= kCols) continue;
-            const size_t ri = (size_t(b) * NJ + (c >> 3)) * 4 + ((c & 7) >> 1);
-            float* rf = reinterpret_cast<float*>(recs + ri);
-            const int u = c & 1;
-            const float w = pw[pl] * s;
-            const float off = (QT == MLB_Q4_0) ? kBmMagicF + static_cast<float>(8 * dsum[pl]) : kBmMagicF;
-            rf[u] = w;
-            rf[2 + u] = -off * w;
-            if constexpr (QT == MLB_Q4_1) reinterpret_cast<float*>(xsums + ri)[u] = pl == 0 ? xsum : 0.0f;
+            for (int pl = 0; pl < 3; ++pl) {
+                const int c = 3 * m + pl;
+                if (c >= kCols) continue;
+                const size_t ri = (size_t(b) * NJ + (c >> 3)) * 4 + ((c & 7) >> 1);
+                float* rf = reinterpret_cast<float*>(recs + ri);
+                const int u = c & 1;
+                const float w = pw[pl] * s;
+                const float off = (QT == MLB_Q4_0) ? kBmMagicF + static_cast<float>(8 * dsum[pl]) : kBmMagicF;
+                rf[u] = w;
+                rf[2 + u] = -off * w;
+                if constexpr (QT == MLB_Q4_1) reinterpret_cast<float*>(xsums + ri)[u] = pl == 0 ? xsum : 0.0f;
+            }
         }
     }
     __syncthreads();
@@ -374,18 +392,17 @@ __global__ void __launch_bounds__(kBmMaxWarps * 32, 1) BlockMmaGemvKernel(const 
     uint8_t* ring = smem;
     uint64_t* bars = reinterpret_cast<uint64_t*>(smem + BmSmem::Ring(npairs, ns, p.stage_bytes));
     volatile int* slot_tiles = reinterpret_cast<volatile int*>(bars + npairs * ns);
-    float* xs = reinterpret_cast<float*>(reinterpret_cast<uint8_t*>(bars) + BmSmem::Bars(npairs, ns));
-    uint2* frags = reinterpret_cast<uint2*>(reinterpret_cast<uint8_t*>(xs) + BmSmem::X(M, p.nb, npairs));
+    uint8_t* scratch_all = reinterpret_cast<uint8_t*>(bars) + BmSmem::Bars(npairs, ns);
+    uint2* frags = reinterpret_cast<uint2*>(scratch_all + BmSmem::Scratch(M, npairs));
     float4* recs = reinterpret_cast<float4*>(reinterpret_cast<uint8_t*>(frags) + BmSmem::Frag(M, p.nb));
     float2* xsums = reinterpret_cast<float2*>(recs + size_t(p.nb) * NJ * 4);
     uint8_t* myring = ring + size_t(pair) * ns * p.stage_bytes;
     uint64_t* mybars = bars + pair * ns;
     volatile int* mytiles = slot_tiles + pair * ns;
-    // after the prologue the x rows' space holds, per pair, the follower's
-    // partial sums (two buffers by tile parity) and the tile's column sums
-    uint8_t* scratch = reinterpret_cast<uint8_t*>(xs) + size_t(pair) * BmSmem::PairScratch(M);
+    // per pair: the follower's partial sums (two buffers by tile parity) and
+    // the tile's column sums
+    uint8_t* scratch = scratch_all + size_t(pair) * BmSmem::PairScratch(M);
     float2* xbuf = reinterpret_cast<float2*>(scratch);
-    float* colsum = reinterpret_cast<float*>(scratch + size_t(NJ) * 2 * 2 * 32 * 8);
 
     const int gp = blockIdx.x * npairs + pair, GP = gridDim.x * npairs;
     const int ustride = p.pitch;
@@ -434,7 +451,7 @@ __global__ void __launch_bounds__(kBmMaxWarps * 32, 1) BlockMmaGemvKernel(const 
                 const uint32_t body = static_cast<uint32_t>(rows * p.rowbytes) & ~15u;
                 if (lane == 0) {
                     MbarExpectTx(bar, body);
-                    BulkLoad(dst, p.w + size_t(row0) * p.rowbytes, body, bar);
+                    BulkLoadHint(dst, p.w + size_t(row0) * p.rowbytes, body, bar, L2EvictFirstPolicy());
                 }
             } else {
                 const int k0 = i_u * p.kc;
@@ -442,8 +459,9 @@ __global__ void __launch_bounds__(kBmMaxWarps * 32, 1) BlockMmaGemvKernel(const 
                 if (lane == 0) MbarExpectTx(bar, seg * rows);
                 __syncwarp();
                 if (lane < rows)
-                    BulkLoad(dst + size_t(lane) * ustride,
-                             p.w + size_t(row0 + lane) * p.rowbytes + size_t(k0) * kBB, seg, bar);
+                    BulkLoadHint(dst + size_t(lane) * ustride,
+                                 p.w + size_t(row0 + lane) * p.rowbytes + size_t(k0) * kBB, seg, bar,
+                                 L2EvictFirstPolicy());
             }
             if (++i_u == p.units_k) {
                 i_u = 0;
@@ -454,20 +472,15 @@ __global__ void __launch_bounds__(kBmMaxWarps * 32, 1) BlockMmaGemvKernel(const 
     };
 
     GridDepWait();
-    {
-        // x first, so its reads are ahead of the weight stream in the memory
-        // queues; then the first units of the ring
-        const int kpad = p.nb * 32;
-        for (int m = 0; m < M; ++m) {
-            StageFloats(xs + m * kpad, p.x + size_t(m) * p.K, p.K);
-            for (int k = p.K + threadIdx.x; k < kpad; k += blockDim.x) xs[m * kpad + k] = 0.0f;
-        }
-        if (leader)
-            for (int s = 0; s < ns; ++s) issue();
-        CpAsyncWaitAll();
-        __syncthreads();
-    }
-    BmBuildTables<QT, M>(xs, p.nb, frags, recs, xsums);  // ends with a CTA barrier: xs is free
+    // x's lines into L2 ahead of the weight stream, then one unit per pair
+    // (x's reads queue behind only half the ring), x's tables, the rest of
+    // the ring
+    for (int i = threadIdx.x; i < (M * p.K + 31) / 32; i += blockDim.x)
+        asm volatile("prefetch.global.L2 [%0];" ::"l"(p.x + size_t(i) * 32));
+    if (leader) issue();
+    BmBuildTables<QT, M>(p.x, p.K, p.nb, frags, recs, xsums);  // ends with a CTA barrier
+    if (leader)
+        for (int s = 1; s < ns; ++s) issue();
     GridDepLaunch();
 
     float2 acc[NJ][2];
@@ -536,17 +549,24 @@ __global__ void __launch_bounds__(kBmMaxWarps * 32, 1) BlockMmaGemvKernel(const 
         }
         if (tile_end) {
             if (leader) {
-                // column sums of the tile: leader + follower partials
-                const float2* xb = xbuf + parity * NJ * 2 * 32;
+                // column sums of the tile: leader + follower partials, written
+                // over the partials once all lanes have read them
+                float2* xb = xbuf + parity * NJ * 2 * 32;
+                float* colsum = reinterpret_cast<float*>(xb);
+#pragma unroll
+                for (int j = 0; j < NJ; ++j) {
+                    acc[j][0] = __fadd2_rn(acc[j][0], xb[(j * 2) * 32 + lane]);
+                    acc[j][1] = __fadd2_rn(acc[j][1], xb[(j * 2 + 1) * 32 + lane]);
+                }
+                __syncwarp();
 #pragma unroll
                 for (int j = 0; j < NJ; ++j) {
 #pragma unroll
                     for (int r = 0; r < 2; ++r) {
-                        const float2 f = xb[(j * 2 + r) * 32 + lane];
                         const int trow = p.rowmap ? 2 * g + r : g + 8 * r;
                         float* cs = colsum + trow * kCols + 8 * j + 2 * t;
-                        cs[0] = acc[j][r].x + f.x;
-                        cs[1] = acc[j][r].y + f.y;
+                        cs[0] = acc[j][r].x;
+                        cs[1] = acc[j][r].y;
                     }
                 }
                 __syncwarp();

@@ -65,10 +65,6 @@ BmPlan PlanBlockMma(BmParams& p, int qtype, int M, int sm_count, int max_smem) {
     if (reinterpret_cast<uintptr_t>(p.w) & 15) return plan;
     // Q8_0 / Q4_0 blocks are read in pairs
     if (qtype != MLB_Q4_1 && (p.nb & 1)) return plan;
-    // below about 1.5 row tiles per SM the weights are too few to stream
-    // (each pair would run its tile's pieces one after another): the other
-    // GEMV splits K across warps instead
-    if (2 * p.tiles < 3 * sm_count) return plan;
     constexpr int kMaxStage = 20 * 1024;
     const long long tile_bytes = 16LL * p.rowbytes;
     if (tile_bytes <= kMaxStage) {
@@ -87,6 +83,11 @@ BmPlan PlanBlockMma(BmParams& p, int qtype, int M, int sm_count, int max_smem) {
     } else {
         return plan;
     }
+    // Too few row tiles to stream: the other GEMV (K split across warps)
+    // finishes sooner below about 4 whole-row tiles per SM, or 1.5 tiles per
+    // SM when rows are split into pieces (each pair would run a tile's
+    // pieces one after another).
+    if (p.units_k == 1 ? p.tiles < 4 * sm_count : 2 * p.tiles < 3 * sm_count) return plan;
     p.rowmap = ((p.pitch / 4) % 4 == 2) ? 1 : 0;
     p.slots = 2;
     constexpr int kMaxPairs = kBmMaxWarps / 2;

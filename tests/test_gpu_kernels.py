@@ -132,14 +132,14 @@ def test_linear_microbench_shapes(mlb, gpu, oracle, qtype, n, k, m):
                         linear_terms(x, bench_dequant(oracle, qtype, n, k)), f"{QNAME[qtype]} [{n},{k}] M={m}")
 
 
-# Shapes of more than 1.5 16-row tiles per SM, which take the tensor-core
-# GEMV over the blocks for 1..8 rows where x's tables fit, covering its unit
-# and bank layouts: K = 4864 (rows split into 8-block pieces copied row by
-# row; 3 and 8 rows of x take the other GEMV), 1024 (16 whole rows per copy,
-# row pitch 0 mod 8 words), 576 (odd pitch in words), 896 (pitch 2 mod 4
-# words: interleaved rows), 800 (odd block count: Q4_1 here, the other GEMV
-# for Q8_0 / Q4_0); N = 4099 ends on a partial tile.
-BLOCK_MMA_SHAPES = [(4099, 4864), (4099, 1024), (4099, 576), (4099, 896), (4099, 800)]
+# Shapes with enough 16-row tiles per SM (1.5 for split rows, 4 for whole
+# rows) to take the tensor-core GEMV over the blocks for 1..8 rows where x's
+# tables fit, covering its unit and bank layouts: K = 4864 (rows split into
+# 8-block pieces copied row by row; 3 and 8 rows of x take the other GEMV),
+# 1024 (16 whole rows per copy, row pitch 0 mod 8 words), 576 (odd pitch in
+# words), 896 (pitch 2 mod 4 words: interleaved rows), 800 (odd block count:
+# Q4_1 here, the other GEMV for Q8_0 / Q4_0); every N ends on a partial tile.
+BLOCK_MMA_SHAPES = [(4099, 4864), (9475, 1024), (9475, 576), (9475, 896), (9475, 800)]
 
 
 @pytest.mark.parametrize("qtype", [Q80, Q40, Q41])
@@ -161,7 +161,7 @@ def test_linear_block_mma_layouts(mlb, gpu, oracle, qtype, n, k):
 def test_linear_block_mma_repeated_calls(mlb, gpu, oracle):
     """The GEMV's tile scheduler resets itself at the end of every launch:
     calls in a row, of different shapes, each give the full result."""
-    cases = [(151936 // 8, 896, 1), (4099, 4864, 1), (4864, 896, 5)]
+    cases = [(151936 // 8, 896, 1), (4099, 4864, 1), (9475, 896, 5)]
     for rep in range(2):
         for (n, k, m) in cases:
             blocks = bench_blocks(oracle, Q80, n, k)
