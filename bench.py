@@ -23,6 +23,10 @@ device); --graph selects the CUDA graph per token instead.
   dropin the reference's own, unchanged forward.cpp device path linked
          against this library (oracle/_ref/forward_on_b200): decode tokens/s
          of 128 greedy tokens after the same prompt
+  tp_batch  batched greedy decoding of the Llama-2-7B architecture (Q4_0)
+         for 64 sequences, 128 prompt ids + 64 tokens, through mlb_batch_*,
+         tensor parallel over all N GPUs (NCCL inside the library): decode
+         tokens/s of the whole job, max over ranks (strong scaling in N)
 With N > 1 (torchrun) every GPU decodes its own sequence (replicas; weak scaling).
 --impl reference times the reference CPU implementation alone, on the same
 config, one line from rank 0.
@@ -260,6 +264,51 @@ def gemv_roofline(lib, dev, torch, stream):
     return algo, per_launch
 
 
+TP_BATCH, TP_PROMPT, TP_NEW = 64, 128, 64
+
+
+def tp_batch_leg(lib, dev, dist, world: int, rank: int):
+    """Batched greedy decoding of the Llama-2-7B architecture (Q4_0, seeded
+    random-init weights) for TP_BATCH sequences of TP_PROMPT uniform prompt ids
+    plus TP_NEW tokens through mlb_batch_*, tensor parallel over all ranks
+    (every linear's rows and the KV heads split world ways, NCCL all-gathers
+    inside the library's captured step; tp_size 1 on one GPU).  Device times
+    from CUDA events on the library stream, maximum over ranks."""
+    import numpy as np
+
+    from mini_llama_b200.batch_bench import MODELS
+    from mini_llama_b200.device import BatchSession, Model, nccl_unique_id
+    from mini_llama_b200.tp import share_nccl_id
+
+    spec = dict(MODELS["llama7b"], max_seq_len=TP_PROMPT + TP_NEW)
+    m = Model(lib, dev, spec)
+    b = None
+    try:
+        m.synthesize(seed=spec["seed"], tied=False)
+        nid = share_nccl_id(dist, lambda: nccl_unique_id(lib)) if world > 1 else None
+        b = BatchSession(m, TP_BATCH, rank, world, nid)
+        rng = np.random.default_rng(spec["seed"] + 1)
+        prompts = rng.integers(0, spec["vocab_size"], size=(TP_BATCH, TP_PROMPT), dtype=np.int32)
+        b.generate(prompts[:, :8], 4)  # warm-up: captures the step graphs
+        toks, pre_ms, dec_ms = b.generate(prompts, TP_NEW)
+        if dist is not None:
+            pre_ms = max_over_ranks(dist, pre_ms, f"cuda:{dev}")
+            dec_ms = max_over_ranks(dist, dec_ms, f"cuda:{dev}")
+        dec_tok = TP_BATCH * (TP_NEW - 1)
+        return {"workload": f"Llama-2-7B-arch Q4_0 random-init, {TP_BATCH} sequences, prompt {TP_PROMPT} + "
+                            f"{TP_NEW} greedy tokens",
+                "path": "mlb_batch_create / mlb_batch_generate",
+                "parallelism": f"tp{world}", "n_gpus": world,
+                "decode_tok_s": dec_tok / (dec_ms / 1e3), "unit": "tokens/s",
+                "ms_per_decode_step": dec_ms / (TP_NEW - 1),
+                "prefill_tok_s": TP_BATCH * TP_PROMPT / (pre_ms / 1e3),
+                "first_tokens": toks[0, :8].tolist()}
+    finally:
+        if b is not None:
+            b.close()
+        m.close()
+
+
 def run_ours(args):
     import numpy as np
     import torch
@@ -393,6 +442,9 @@ def run_ours(args):
 
     sess.close()
     model.close()
+    tp = None
+    if not args.no_tp:
+        tp = tp_batch_leg(lib, dev, dist, world, rank)
     if dist is not None:
         dist.barrier()
         dist.destroy_process_group()
@@ -432,6 +484,7 @@ def run_ours(args):
         "cpu_baseline": cpu,
         "prefill": prefill,
         "dropin": dropin,
+        "tp_batch": tp,
         "clocks": clk,
         "gpu_launches": gpu_launches,
     }
@@ -449,6 +502,8 @@ def main():
     ap.add_argument("--no-e2e", action="store_true")
     ap.add_argument("--no-dropin", action="store_true",
                     help="skip the reference forward.cpp on this library (builds the model on the CPU)")
+    ap.add_argument("--no-tp", action="store_true",
+                    help="skip the tensor-parallel batched Llama-2-7B leg")
     ap.add_argument("--no-prefill", action="store_true",
                     help="profiling: skip the 64-token prefill (KV cache left empty)")
     ap.add_argument("--graph", action="store_true",
