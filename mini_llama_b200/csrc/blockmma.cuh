@@ -5,17 +5,17 @@
 // Work: a row tile is 16 consecutive weight rows; a unit is one row tile over
 // kc consecutive blocks (kc = all blocks of the row when 16 rows fit a slot,
 // else a multiple of 8, so every piece of a row starts 16-byte aligned).  A
-// pair of warps owns whole row tiles (all their units in turn) and its own
-// ring of shared-memory slots; the leader moves a whole-row unit with one bulk
-// copy (16 GGUF rows are contiguous), a split unit with one bulk copy per row
-// (lanes 0..15), completing on the slot's mbarrier; weights are read once, so
-// the copies mark their lines first to leave the L2.  The two warps split each
-// unit's blocks in halves and meet at one named barrier per unit (after which
-// the slot is refilled), adding the follower's partial sums at the end of a
-// tile.  Each pair starts on two fixed tiles and then takes the next free tile
+// group of 2 or 4 warps owns whole row tiles (all their units in turn) and its
+// own ring of shared-memory slots; the leader moves a whole-row unit with one
+// bulk copy (16 GGUF rows are contiguous), a split unit with one bulk copy per
+// row (lanes 0..15), completing on the slot's mbarrier; weights are read once,
+// so the copies mark their lines first to leave the L2.  The group's warps
+// split each unit's blocks and meet at one named barrier per unit (after which
+// the slot is refilled), adding the followers' partial sums at the end of a
+// tile.  Each group starts on two fixed tiles and then takes the next free tile
 // from a device counter (fetched one tile ahead, so its latency hides behind a
-// tile of work), so pairs that run faster take more tiles and all finish
-// within about one tile of each other.  After the prologue no pair waits on
+// tile of work), so groups that run faster take more tiles and all finish
+// within about one tile of each other.  After the prologue no group waits on
 // another.
 //
 // MMA operands: A = the quants of one block column of the tile, read from the
@@ -46,7 +46,7 @@
 
 namespace mlb {
 
-constexpr int kBmMaxWarps = 16;  // 8 warp pairs
+constexpr int kBmMaxWarps = 16;
 constexpr uint32_t kBmMagic = 0x4B400000u;  // 1.5 * 2^23
 constexpr float kBmMagicF = 12582912.0f;
 
@@ -67,7 +67,8 @@ struct BmParams {
     int kc;         // blocks per unit
     int units_k;    // units per row tile (1: whole rows)
     int tiles;      // row tiles
-    int slots;      // ring slots per warp
+    int slots;      // ring slots per warp group
+    int gsize;      // warps per group (2 or 4): they split each unit's blocks
     int stage_bytes;
     int pitch;      // bytes from one row of a unit to the next in shared memory
     int rowmap;     // 1: MMA rows g, g + 8 are tile rows 2g, 2g + 1; 0: g, g + 8
@@ -92,29 +93,35 @@ struct BmTraits<MLB_Q4_1> {
     static constexpr bool kUnsigned = true;
 };
 
-// Shared memory: slots [pairs][slots][stage_bytes] | mbarriers [pairs][slots]
-// | slot tile numbers [pairs][slots] int | per pair the follower's partial
-// sums [2][NJ][2][32] float2 (the buffer just read then holds the tile's
-// column sums [16][8 NJ] floats) | B fragments [nb][NJ][32] uint2 |
+// Shared memory: slots [groups][slots][stage_bytes] | mbarriers
+// [groups][slots] | slot tile numbers [groups][slots] int | per group the
+// followers' partial sums [2][gsize - 1][NJ][2][32] float2 (the parity buffer
+// just read then holds the tile's column sums [16][8 NJ] floats) | B
+// fragments [nb][NJ][32] uint2 |
 // column records [nb][NJ][4] float4 | Q4_1: x block sums [nb][NJ][4] float2.
 struct BmSmem {
-    static __host__ __device__ size_t Ring(int pairs, int slots, int stage_bytes) {
-        return size_t(pairs) * slots * stage_bytes;
+    static __host__ __device__ size_t Ring(int groups, int slots, int stage_bytes) {
+        return size_t(groups) * slots * stage_bytes;
     }
-    static __host__ __device__ size_t Bars(int pairs, int slots) {
-        return (size_t(pairs) * slots * 12 + 15) & ~size_t(15);
+    static __host__ __device__ size_t Bars(int groups, int slots) {
+        return (size_t(groups) * slots * 12 + 15) & ~size_t(15);
     }
-    // two buffers (tile parity) of [NJ][2][32] float2; the leader turns the
-    // one it has read into the tile's column sums [16][8 NJ] floats
-    static __host__ __device__ size_t PairScratch(int M) { return size_t(BmMmas(M)) * 2 * 2 * 32 * 8; }
-    static __host__ __device__ size_t Scratch(int M, int pairs) { return size_t(pairs) * PairScratch(M); }
+    // two buffers (tile parity) of [gsize - 1][NJ][2][32] float2; the leader
+    // turns the one it has read into the tile's column sums [16][8 NJ] floats
+    static __host__ __device__ size_t GroupScratch(int M, int gsize) {
+        return size_t(BmMmas(M)) * 2 * (gsize - 1) * 2 * 32 * 8;
+    }
+    static __host__ __device__ size_t Scratch(int M, int groups, int gsize) {
+        return size_t(groups) * GroupScratch(M, gsize);
+    }
     static __host__ __device__ size_t Frag(int M, int nb) { return size_t(nb) * BmMmas(M) * 256; }
     // records (float4), then for Q4_1 the x block sums (float2)
     static __host__ __device__ size_t Rec(int M, int nb, bool sums) {
         return size_t(nb) * BmMmas(M) * (sums ? 64 + 32 : 64);
     }
-    static __host__ __device__ size_t Bytes(int M, int nb, int pairs, int slots, int stage_bytes, bool sums) {
-        return Ring(pairs, slots, stage_bytes) + Bars(pairs, slots) + Scratch(M, pairs) + Frag(M, nb) +
+    static __host__ __device__ size_t Bytes(int M, int nb, int groups, int slots, int stage_bytes, bool sums,
+                                            int gsize) {
+        return Ring(groups, slots, stage_bytes) + Bars(groups, slots) + Scratch(M, groups, gsize) + Frag(M, nb) +
                Rec(M, nb, sums);
     }
 };
@@ -261,15 +268,15 @@ __device__ __forceinline__ void BmUnit(const uint8_t* unit, int ustride, int row
     }
 }
 
-// Barrier of the two warps of a pair (named barrier id, 64 threads) that also
-// ORs a flag over them, so both take the same branch after it.
-__device__ __forceinline__ bool PairBarrierOr(int id, bool flag) {
+// Barrier of the warps of a group (named barrier id, `threads` threads) that
+// also ORs a flag over them, so all take the same branch after it.
+__device__ __forceinline__ bool GroupBarrierOr(int id, int threads, bool flag) {
     uint32_t r;
     asm volatile(
-        "{\n .reg .pred p, q;\n setp.ne.u32 q, %1, 0;\n bar.red.or.pred p, %2, 64, q;\n"
+        "{\n .reg .pred p, q;\n setp.ne.u32 q, %1, 0;\n bar.red.or.pred p, %2, %3, q;\n"
         " selp.u32 %0, 1, 0, p;\n}\n"
         : "=r"(r)
-        : "r"(static_cast<uint32_t>(flag)), "r"(id)
+        : "r"(static_cast<uint32_t>(flag)), "r"(id), "r"(threads)
         : "memory");
     return r != 0;
 }
@@ -384,27 +391,29 @@ __global__ void __launch_bounds__(kBmMaxWarps * 32, 1) BlockMmaGemvKernel(const 
     constexpr int kCols = 8 * NJ;
     constexpr int kBB = BmTraits<QT>::kBytes;
     extern __shared__ __align__(128) uint8_t smem[];
-    const int nw = blockDim.x >> 5, npairs = nw >> 1;
+    const int gs = p.gsize;
+    const int nw = blockDim.x >> 5, ngroups = nw / gs;  // warp groups
     const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31, g = lane >> 2, t = lane & 3;
-    const int pair = warp >> 1;
-    const bool leader = (warp & 1) == 0;
+    const int grp = warp / gs, member = warp - grp * gs;
+    const bool leader = member == 0;
     const int ns = p.slots;
     uint8_t* ring = smem;
-    uint64_t* bars = reinterpret_cast<uint64_t*>(smem + BmSmem::Ring(npairs, ns, p.stage_bytes));
-    volatile int* slot_tiles = reinterpret_cast<volatile int*>(bars + npairs * ns);
-    uint8_t* scratch_all = reinterpret_cast<uint8_t*>(bars) + BmSmem::Bars(npairs, ns);
-    uint2* frags = reinterpret_cast<uint2*>(scratch_all + BmSmem::Scratch(M, npairs));
+    uint64_t* bars = reinterpret_cast<uint64_t*>(smem + BmSmem::Ring(ngroups, ns, p.stage_bytes));
+    volatile int* slot_tiles = reinterpret_cast<volatile int*>(bars + ngroups * ns);
+    uint8_t* scratch_all = reinterpret_cast<uint8_t*>(bars) + BmSmem::Bars(ngroups, ns);
+    uint2* frags = reinterpret_cast<uint2*>(scratch_all + BmSmem::Scratch(M, ngroups, gs));
     float4* recs = reinterpret_cast<float4*>(reinterpret_cast<uint8_t*>(frags) + BmSmem::Frag(M, p.nb));
     float2* xsums = reinterpret_cast<float2*>(recs + size_t(p.nb) * NJ * 4);
-    uint8_t* myring = ring + size_t(pair) * ns * p.stage_bytes;
-    uint64_t* mybars = bars + pair * ns;
-    volatile int* mytiles = slot_tiles + pair * ns;
-    // per pair: the follower's partial sums (two buffers by tile parity) and
+    uint8_t* myring = ring + size_t(grp) * ns * p.stage_bytes;
+    uint64_t* mybars = bars + grp * ns;
+    volatile int* mytiles = slot_tiles + grp * ns;
+    // per group: the followers' partial sums (two buffers by tile parity) and
     // the tile's column sums
-    uint8_t* scratch = scratch_all + size_t(pair) * BmSmem::PairScratch(M);
+    uint8_t* scratch = scratch_all + size_t(grp) * BmSmem::GroupScratch(M, gs);
     float2* xbuf = reinterpret_cast<float2*>(scratch);
+    const int xpar = (gs - 1) * NJ * 2 * 32;  // float2 per parity buffer
 
-    const int gp = blockIdx.x * npairs + pair, GP = gridDim.x * npairs;
+    const int gp = blockIdx.x * ngroups + grp, GP = gridDim.x * ngroups;
     const int ustride = p.pitch;
 
     if (leader && lane == 0) {
@@ -437,7 +446,7 @@ __global__ void __launch_bounds__(kBmMaxWarps * 32, 1) BlockMmaGemvKernel(const 
         uint64_t* bar = &mybars[i_slot];
         ++inflight;
         if (i_tile >= p.tiles) {
-            // no more tiles: a phase without data tells the pair to stop
+            // no more tiles: a phase without data tells the group to stop
             if (lane == 0) {
                 mytiles[i_slot] = -1;
                 asm volatile("mbarrier.arrive.shared::cta.b64 _, [%0];" ::"r"(SmemAddr(bar)) : "memory");
@@ -472,7 +481,7 @@ __global__ void __launch_bounds__(kBmMaxWarps * 32, 1) BlockMmaGemvKernel(const 
     };
 
     GridDepWait();
-    // x's lines into L2 ahead of the weight stream, then one unit per pair
+    // x's lines into L2 ahead of the weight stream, then one unit per group
     // (x's reads queue behind only half the ring), x's tables, the rest of
     // the ring
     for (int i = threadIdx.x; i < (M * p.K + 31) / 32; i += blockDim.x)
@@ -506,13 +515,20 @@ __global__ void __launch_bounds__(kBmMaxWarps * 32, 1) BlockMmaGemvKernel(const 
                     __syncwarp();
                 }
             }
-            // the leader takes the first half of the unit's blocks
+            // member r of the group takes blocks [b_r, b_{r+1}) of the unit
+            // (whole block pairs for Q8_0 / Q4_0)
             const int k0 = c_u * p.kc, kcc = min(p.kc, p.nb - k0);
-            const int half = (QT == MLB_Q4_1) ? (kcc + 1) / 2 : (kcc + 2) / 4 * 2;
-            BmUnit<QT, NJ>(unit, ustride, p.rowmap, leader ? 0 : half, leader ? half : kcc, k0, frags, recs,
-                           xsums, lane, acc);
+            int i0, i1;
+            if (QT == MLB_Q4_1) {
+                i0 = kcc * member / gs;
+                i1 = kcc * (member + 1) / gs;
+            } else {
+                i0 = (kcc / 2) * member / gs * 2;
+                i1 = (kcc / 2) * (member + 1) / gs * 2;
+            }
+            BmUnit<QT, NJ>(unit, ustride, p.rowmap, i0, i1, k0, frags, recs, xsums, lane, acc);
             if (tile_end && !leader) {
-                float2* xb = xbuf + parity * NJ * 2 * 32;
+                float2* xb = xbuf + parity * xpar + (member - 1) * NJ * 2 * 32;
 #pragma unroll
                 for (int j = 0; j < NJ; ++j) {
                     xb[(j * 2) * 32 + lane] = acc[j][0];
@@ -520,9 +536,9 @@ __global__ void __launch_bounds__(kBmMaxWarps * 32, 1) BlockMmaGemvKernel(const 
                 }
             }
         }
-        // both warps have read the slot; either both go on or both stop (at
-        // the stop mark, or when either warp's wait expired)
-        if (PairBarrierOr(1 + pair, !run)) {
+        // the group has read the slot; either all go on or all stop (at the
+        // stop mark, or when any warp's wait expired)
+        if (GroupBarrierOr(1 + grp, 32 * gs, !run)) {
             if (!ok && lane == 0 && p.status) atomicExch(p.status, MLB_ERR_DEVICE_TIMEOUT);
             // leave no copy in flight into shared memory: wait (bounded) for
             // the other issued units (none after the stop mark), then stop
@@ -549,14 +565,17 @@ __global__ void __launch_bounds__(kBmMaxWarps * 32, 1) BlockMmaGemvKernel(const 
         }
         if (tile_end) {
             if (leader) {
-                // column sums of the tile: leader + follower partials, written
-                // over the partials once all lanes have read them
-                float2* xb = xbuf + parity * NJ * 2 * 32;
+                // column sums of the tile: leader + follower partials (in
+                // member order), written over the partials once all lanes
+                // have read them
+                float2* xb = xbuf + parity * xpar;
                 float* colsum = reinterpret_cast<float*>(xb);
+                for (int f = 0; f < gs - 1; ++f) {
 #pragma unroll
-                for (int j = 0; j < NJ; ++j) {
-                    acc[j][0] = __fadd2_rn(acc[j][0], xb[(j * 2) * 32 + lane]);
-                    acc[j][1] = __fadd2_rn(acc[j][1], xb[(j * 2 + 1) * 32 + lane]);
+                    for (int j = 0; j < NJ; ++j) {
+                        acc[j][0] = __fadd2_rn(acc[j][0], xb[(f * NJ + j) * 2 * 32 + lane]);
+                        acc[j][1] = __fadd2_rn(acc[j][1], xb[((f * NJ + j) * 2 + 1) * 32 + lane]);
+                    }
                 }
                 __syncwarp();
 #pragma unroll

@@ -89,19 +89,22 @@ BmPlan PlanBlockMma(BmParams& p, int qtype, int M, int sm_count, int max_smem) {
     // pieces one after another).
     if (p.units_k == 1 ? p.tiles < 4 * sm_count : 2 * p.tiles < 3 * sm_count) return plan;
     p.rowmap = ((p.pitch / 4) % 4 == 2) ? 1 : 0;
+    // Warp pairs with a two-slot ring each (groups of 4 warps with 3 or 4
+    // slots, splitting each tile 4 ways, measured slower at every row count)
+    p.gsize = 2;
     p.slots = 2;
-    constexpr int kMaxPairs = kBmMaxWarps / 2;
+    const bool sums = qtype == MLB_Q4_1;
     const size_t budget = static_cast<size_t>(max_smem) - 1024;
     plan.grid = sm_count;
-    // as many pairs as fit (the tile scheduler balances them), at most one per
-    // tile of an SM's share
-    int pairs = std::min(kMaxPairs, (p.tiles + plan.grid - 1) / plan.grid);
-    while (pairs > 0 && BmSmem::Bytes(M, p.nb, pairs, p.slots, p.stage_bytes, qtype == MLB_Q4_1) > budget) --pairs;
-    // x's tables span all of K: when they leave room for fewer than three
-    // pairs (long rows, many rows of x), too few copies are in flight
-    if (pairs < std::min(3, (p.tiles + plan.grid - 1) / plan.grid)) return plan;
-    plan.warps = 2 * pairs;
-    plan.smem = BmSmem::Bytes(M, p.nb, pairs, p.slots, p.stage_bytes, qtype == MLB_Q4_1);
+    // as many groups as fit (the tile scheduler balances them), at most one
+    // per tile of an SM's share
+    int groups = std::min(kBmMaxWarps / p.gsize, (p.tiles + plan.grid - 1) / plan.grid);
+    while (groups > 0 && BmSmem::Bytes(M, p.nb, groups, p.slots, p.stage_bytes, sums, p.gsize) > budget) --groups;
+    // x's tables span all of K: when they leave room for fewer than six
+    // warps (long rows, many rows of x), too few copies are in flight
+    if (groups * p.gsize < std::min(6, p.gsize * ((p.tiles + plan.grid - 1) / plan.grid))) return plan;
+    plan.warps = groups * p.gsize;
+    plan.smem = BmSmem::Bytes(M, p.nb, groups, p.slots, p.stage_bytes, sums, p.gsize);
     plan.ok = plan.smem <= budget;
     return plan;
 }
