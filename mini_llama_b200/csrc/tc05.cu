@@ -113,9 +113,26 @@ __global__ void __launch_bounds__(128) TcPrepX(const float* x, int M, int K, int
     const int mt = row / MX, r = row % MX;
     const bool live = row < M;
     const float* xr = x + size_t(live ? row : 0) * K;
+    const bool vec = (K & 3) == 0 && (reinterpret_cast<uintptr_t>(x) & 15) == 0;
+    // rows of up to 4 x 128 8-element chunks stay in registers (chunk
+    // tid + 128 j in va[j], vb[j]): x is read once
+    constexpr int kRegChunks = 4;
+    const bool inreg = vec && kst * 2 <= kRegChunks * 128;
+    float4 va[kRegChunks], vb[kRegChunks];
     float mx = 0.0f;
-    if (live)
+    if (inreg) {
+#pragma unroll
+        for (int j = 0; j < kRegChunks; ++j) {
+            const int k0 = 8 * (tid + 128 * j);
+            const float4 z = make_float4(0.0f, 0.0f, 0.0f, 0.0f);
+            va[j] = (live && k0 + 4 <= K) ? *reinterpret_cast<const float4*>(xr + k0) : z;
+            vb[j] = (live && k0 + 8 <= K) ? *reinterpret_cast<const float4*>(xr + k0 + 4) : z;
+            mx = fmaxf(mx, fmaxf(fmaxf(fabsf(va[j].x), fabsf(va[j].y)), fmaxf(fabsf(va[j].z), fabsf(va[j].w))));
+            mx = fmaxf(mx, fmaxf(fmaxf(fabsf(vb[j].x), fabsf(vb[j].y)), fmaxf(fabsf(vb[j].z), fabsf(vb[j].w))));
+        }
+    } else if (live) {
         for (int k = tid; k < K; k += 128) mx = fmaxf(mx, fabsf(xr[k]));
+    }
     mx = WarpMax(mx);
     if ((tid & 31) == 0) red[tid >> 5] = mx;
     __syncthreads();
@@ -124,11 +141,19 @@ __global__ void __launch_bounds__(128) TcPrepX(const float* x, int M, int K, int
     const float sc = live ? Pow2(s) : 0.0f;
     if (live && tid == 0) xundo[row] = Pow2(-s);
     const size_t img = size_t(MX) * kTcK * 2;  // bytes of one image
-    const bool vec = (K & 3) == 0 && (reinterpret_cast<uintptr_t>(x) & 15) == 0;
-    for (int ch = tid; ch < kst * 2; ch += 128) {
+    for (int ch = tid, j = 0; ch < kst * 2; ch += 128, ++j) {
         const int kt = ch >> 1, c = ch & 1, k0 = kt * kTcK + c * 8;
         float v[8];
-        if (live && vec && k0 + 8 <= K) {
+        if (inreg) {
+            float4 a = va[0], b = vb[0];
+#pragma unroll
+            for (int q = 1; q < kRegChunks; ++q)
+                if (j == q) {
+                    a = va[q];
+                    b = vb[q];
+                }
+            v[0] = a.x; v[1] = a.y; v[2] = a.z; v[3] = a.w; v[4] = b.x; v[5] = b.y; v[6] = b.z; v[7] = b.w;
+        } else if (live && vec && k0 + 8 <= K) {
             const float4 a = *reinterpret_cast<const float4*>(xr + k0);
             const float4 b = *reinterpret_cast<const float4*>(xr + k0 + 4);
             v[0] = a.x; v[1] = a.y; v[2] = a.z; v[3] = a.w; v[4] = b.x; v[5] = b.y; v[6] = b.z; v[7] = b.w;
@@ -156,6 +181,25 @@ __global__ void __launch_bounds__(256) TcReduce(const float* part, int splits, i
                                                 float* y) {
     const size_t mn = size_t(M) * N;
     GridDepWait();
+    if ((N & 3) == 0 && mn < (size_t(1) << 32) &&
+        ((reinterpret_cast<uintptr_t>(part) | reinterpret_cast<uintptr_t>(y) | reinterpret_cast<uintptr_t>(bias)) & 15) == 0) {
+        // four columns per thread (the same sum order per element)
+        const uint32_t mn4 = static_cast<uint32_t>(mn >> 2), n4 = static_cast<uint32_t>(N >> 2);
+        const float4* p4 = reinterpret_cast<const float4*>(part);
+        for (uint32_t i = blockIdx.x * blockDim.x + threadIdx.x; i < mn4; i += gridDim.x * blockDim.x) {
+            float4 acc = bias ? reinterpret_cast<const float4*>(bias)[i % n4] : make_float4(0.0f, 0.0f, 0.0f, 0.0f);
+#pragma unroll 8
+            for (int s = 0; s < splits; ++s) {
+                const float4 v = __ldg(p4 + size_t(s) * mn4 + i);
+                acc.x += v.x;
+                acc.y += v.y;
+                acc.z += v.z;
+                acc.w += v.w;
+            }
+            reinterpret_cast<float4*>(y)[i] = acc;
+        }
+        return;
+    }
     for (size_t i = blockIdx.x * size_t(blockDim.x) + threadIdx.x; i < mn; i += size_t(gridDim.x) * blockDim.x) {
         float acc = bias ? bias[i % N] : 0.0f;
 #pragma unroll 8
