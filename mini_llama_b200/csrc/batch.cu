@@ -247,8 +247,10 @@ void CaptureBatchStep(mlb_batch* s, DeviceContext& c) {
     int* status = s->state + 2;
     cudaStream_t st = c.stream;
     auto F = [&](int l, int kind) { return static_cast<const float*>(m->Ptr(m->Get(l, kind))); };
-    auto linear = [&](const float* x, const uint8_t* w, int K, int N, const float* bias, float* y) {
-        LinearRows(c, qt, x, w, B, K, N, bias, y, s->tc_ws);
+    // same_x: x is the previous linear's input, unchanged (its x images are reused)
+    auto linear = [&](const float* x, const uint8_t* w, int K, int N, const float* bias, float* y,
+                      bool same_x = false) {
+        LinearRows(c, qt, x, w, B, K, N, bias, y, s->tc_ws, same_x);
     };
     // rank-sliced rows -> whole rows on every rank (plus `add` when given)
     auto gather = [&](const float* local, int n_local, const float* add, float* dst) {
@@ -275,8 +277,8 @@ void CaptureBatchStep(mlb_batch* s, DeviceContext& c) {
             const float* bk = cf.qkv_bias ? F(l, MLB_W_BK) + size_t(s->k0) * hd : nullptr;
             const float* bv = cf.qkv_bias ? F(l, MLB_W_BV) + size_t(s->k0) * hd : nullptr;
             linear(s->xn, Rows(m, l, MLB_W_WQ, s->h0 * hd, cf.dim), cf.dim, qd_l, bq, s->q);
-            linear(s->xn, Rows(m, l, MLB_W_WK, s->k0 * hd, cf.dim), cf.dim, kd_l, bk, s->k);
-            linear(s->xn, Rows(m, l, MLB_W_WV, s->k0 * hd, cf.dim), cf.dim, kd_l, bv, s->v);
+            linear(s->xn, Rows(m, l, MLB_W_WK, s->k0 * hd, cf.dim), cf.dim, kd_l, bk, s->k, true);
+            linear(s->xn, Rows(m, l, MLB_W_WV, s->k0 * hd, cf.dim), cf.dim, kd_l, bv, s->v, true);
             // 2. RoPE + KV write + split-K attention over this rank's KV heads
             {
                 AttnParams a = {};
@@ -320,7 +322,7 @@ void CaptureBatchStep(mlb_batch* s, DeviceContext& c) {
             Launch("RowsRmsNormKernel", RowsRmsNormKernel, dim3(B), dim3(kRowThreads), 0, st, true,
                    const_cast<const float*>(s->xmid), F(l, MLB_W_FFN_NORM), s->xn, cf.dim, cf.rms_norm_eps);
             linear(s->xn, Rows(m, l, MLB_W_GATE, s->f0, cf.dim), cf.dim, fl, nullptr, s->gate);
-            linear(s->xn, Rows(m, l, MLB_W_UP, s->f0, cf.dim), cf.dim, fl, nullptr, s->up);
+            linear(s->xn, Rows(m, l, MLB_W_UP, s->f0, cf.dim), cf.dim, fl, nullptr, s->up, true);
             Launch("RowsSwigluKernel", RowsSwigluKernel, dim3(GridFor(size_t(B) * fl, 256, c.sm_count)), dim3(256), 0, st,
                    true, const_cast<const float*>(s->gate), const_cast<const float*>(s->up), size_t(B) * fl,
                    s->sw_l);

@@ -71,6 +71,11 @@ struct DeviceContext {
     void* pinned = nullptr;  // small pinned staging buffer for host<->device scalars
     size_t pinned_bytes = 0;
     int* status = nullptr;   // device status word of the op kernels with bounded waits
+    // the x images the tensor-core linear's pre-pass last wrote (on this
+    // context's stream): input, workspace and their shape
+    const void* tc_x = nullptr;
+    const void* tc_ws = nullptr;
+    int tc_m = 0, tc_k = 0, tc_mx = 0, tc_mtiles = 0;
 };
 
 DeviceContext& Ctx(int device);                     // creates on first use, makes device current

@@ -243,9 +243,9 @@ void QuantLinear(const char* caller, int device, int qtype, const float* x, cons
 }
 
 void LinearRows(DeviceContext& c, int qtype, const float* x, const uint8_t* wb, int rows, int in_features,
-                int out_features, const float* bias, float* y, void* tc_workspace) {
+                int out_features, const float* bias, float* y, void* tc_workspace, bool reuse_x) {
     if (rows >= kTcMinRows) {  // prefill-sized batches: tcgen05 tensor cores
-        LaunchTcLinear(c, qtype, x, wb, rows, in_features, out_features, bias, y, c.status, tc_workspace);
+        LaunchTcLinear(c, qtype, x, wb, rows, in_features, out_features, bias, y, c.status, tc_workspace, reuse_x);
         return;
     }
 

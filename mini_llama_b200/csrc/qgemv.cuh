@@ -546,15 +546,18 @@ struct GemvPlan {
 // caller that captures the launch into a CUDA graph owns it), or null for the
 // context's grow-only workspace.
 constexpr int kTcMinRows = kGemvMaxM + 1;
+// reuse_x: x and the workspace are those of the previous call on this stream
+// and x has not changed since, so that call's x images are reused when the
+// shapes match (the pre-pass is skipped); any mismatch runs the pre-pass.
 void LaunchTcLinear(DeviceContext& c, int qtype, const float* x, const uint8_t* w, int M, int K, int N,
-                    const float* bias, float* y, int* status, void* workspace = nullptr);
+                    const float* bias, float* y, int* status, void* workspace = nullptr, bool reuse_x = false);
 size_t TcWorkspaceBytes(int M, int K, int N, int sm_count);
 
 // Quantized linear over GGUF blocks for any row count (the GEMV up to
 // kGemvMaxM rows at a time below kTcMinRows, the tensor cores above), on the
 // context's stream; tc_workspace as for LaunchTcLinear.
 void LinearRows(DeviceContext& c, int qtype, const float* x, const uint8_t* w, int rows, int K, int N,
-                const float* bias, float* y, void* tc_workspace = nullptr);
+                const float* bias, float* y, void* tc_workspace = nullptr, bool reuse_x = false);
 
 // M = 1 launch of a decode-graph variant (pro/epi are GemvPrologue/GemvEpilogue).
 void LaunchGemvDecode(int qtype, int pro, int epi, const GemvParams& p, const GemvPlan& plan,

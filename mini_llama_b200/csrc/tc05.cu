@@ -894,7 +894,7 @@ TcLayout LayoutTc(int M, int K, int N, int sms) {
 
 template <int QT>
 void LaunchTcT(DeviceContext& c, const float* x, const uint8_t* w, int M, int K, int N, const float* bias,
-               float* y, int* status, void* workspace) {
+               float* y, int* status, void* workspace, bool reuse_x) {
     const TcLayout L = LayoutTc(M, K, N, c.sm_count);
     const TcPlan& p = L.plan;
     const int nb = L.nb, kst = L.kst;
@@ -902,7 +902,17 @@ void LaunchTcT(DeviceContext& c, const float* x, const uint8_t* w, int M, int K,
     uint8_t* ws = static_cast<uint8_t*>(workspace ? workspace : Workspace(c, L.total));
     float* undo = reinterpret_cast<float*>(ws + undo_off);
     float* part = reinterpret_cast<float*>(ws + part_off);
-    Launch("TcPrepX", TcPrepX, dim3(p.mtiles * p.mx), dim3(128), 0, c.stream, true, x, M, K, p.mx, kst, undo, ws);
+    const bool reuse = reuse_x && c.tc_x == x && c.tc_ws == ws && c.tc_m == M && c.tc_k == K &&
+                       c.tc_mx == p.mx && c.tc_mtiles == p.mtiles;
+    if (!reuse)
+        Launch("TcPrepX", TcPrepX, dim3(p.mtiles * p.mx), dim3(128), 0, c.stream, true, x, M, K, p.mx, kst, undo,
+               ws);
+    c.tc_x = x;
+    c.tc_ws = ws;
+    c.tc_m = M;
+    c.tc_k = K;
+    c.tc_mx = p.mx;
+    c.tc_mtiles = p.mtiles;
     TcArgs a{w, N, K, nb, M, p.mx, p.mtiles, kst, p.kper, ws, undo, bias, y, part, p.splits, status, 0};
     const dim3 grid(p.mtiles * p.splits, (N + p.nw * kTcRows - 1) / (p.nw * kTcRows));
     CUtensorMap wmap;
@@ -923,13 +933,13 @@ void LaunchTcT(DeviceContext& c, const float* x, const uint8_t* w, int M, int K,
 size_t TcWorkspaceBytes(int M, int K, int N, int sm_count) { return LayoutTc(M, K, N, sm_count).total; }
 
 void LaunchTcLinear(DeviceContext& c, int qtype, const float* x, const uint8_t* w, int M, int K, int N,
-                    const float* bias, float* y, int* status, void* workspace) {
+                    const float* bias, float* y, int* status, void* workspace, bool reuse_x) {
     static_assert(sizeof(TcShared) <= kTcHeader, "shared header");
     Require((reinterpret_cast<uintptr_t>(w) & 1) == 0, "mlb_quant_linear", "weight blocks must be 2-byte aligned");
     switch (qtype) {
-        case MLB_Q8_0: LaunchTcT<MLB_Q8_0>(c, x, w, M, K, N, bias, y, status, workspace); break;
-        case MLB_Q4_0: LaunchTcT<MLB_Q4_0>(c, x, w, M, K, N, bias, y, status, workspace); break;
-        default: LaunchTcT<MLB_Q4_1>(c, x, w, M, K, N, bias, y, status, workspace); break;
+        case MLB_Q8_0: LaunchTcT<MLB_Q8_0>(c, x, w, M, K, N, bias, y, status, workspace, reuse_x); break;
+        case MLB_Q4_0: LaunchTcT<MLB_Q4_0>(c, x, w, M, K, N, bias, y, status, workspace, reuse_x); break;
+        default: LaunchTcT<MLB_Q4_1>(c, x, w, M, K, N, bias, y, status, workspace, reuse_x); break;
     }
 }
 
