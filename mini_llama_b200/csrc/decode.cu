@@ -636,8 +636,10 @@ void Prefill(mlb_session* s, DeviceContext& c, int start, int n) {
     auto W = [&](int l, int kind) { return static_cast<const uint8_t*>(m->Ptr(m->Get(l, kind))); };
     auto Fv = [&](int l, int kind) { return static_cast<const float*>(m->Ptr(m->Get(l, kind))); };
     // (not captured into a graph: the tensor-core linears use the context's workspace)
-    auto linear = [&](const float* x, const uint8_t* w, int rows, int K, int N, const float* bias, float* y) {
-        LinearRows(c, qt, x, w, rows, K, N, bias, y);
+    // same_x: x is the previous linear's input, unchanged (its x images are reused)
+    auto linear = [&](const float* x, const uint8_t* w, int rows, int K, int N, const float* bias, float* y,
+                      bool same_x = false) {
+        LinearRows(c, qt, x, w, rows, K, N, bias, y, nullptr, same_x);
     };
     auto rms = [&](const float* x, const float* w, float* y, int rows) {
         Launch("RowsRmsNormKernel", RowsRmsNormKernel, dim3(rows), dim3(256), 0, st, true, x, w, y, D,
@@ -655,8 +657,8 @@ void Prefill(mlb_session* s, DeviceContext& c, int start, int n) {
     for (int l = 0; l < cf.n_layers; ++l) {
         rms(s->pf_x, Fv(l, MLB_W_ATTN_NORM), s->pf_xn, n);
         linear(s->pf_xn, W(l, MLB_W_WQ), n, D, qd, cf.qkv_bias ? Fv(l, MLB_W_BQ) : nullptr, s->pf_q);
-        linear(s->pf_xn, W(l, MLB_W_WK), n, D, kd, cf.qkv_bias ? Fv(l, MLB_W_BK) : nullptr, s->pf_k);
-        linear(s->pf_xn, W(l, MLB_W_WV), n, D, kd, cf.qkv_bias ? Fv(l, MLB_W_BV) : nullptr, s->pf_v);
+        linear(s->pf_xn, W(l, MLB_W_WK), n, D, kd, cf.qkv_bias ? Fv(l, MLB_W_BK) : nullptr, s->pf_k, true);
+        linear(s->pf_xn, W(l, MLB_W_WV), n, D, kd, cf.qkv_bias ? Fv(l, MLB_W_BV) : nullptr, s->pf_v, true);
         Launch("RowsRopeKvKernel", RowsRopeKvKernel, dim3(n), dim3(256), 0, st, true, s->pf_q,
                const_cast<const float*>(s->pf_k), const_cast<const float*>(s->pf_v), cf.n_heads, cf.n_kv_heads, hd,
                start, const_cast<const float*>(m->rope_cos), const_cast<const float*>(m->rope_sin),
@@ -691,7 +693,7 @@ void Prefill(mlb_session* s, DeviceContext& c, int start, int n) {
         add(s->pf_x, s->pf_o, s->pf_xmid, size_t(n) * D);
         rms(s->pf_xmid, Fv(l, MLB_W_FFN_NORM), s->pf_xn, n);
         linear(s->pf_xn, W(l, MLB_W_GATE), n, D, F, nullptr, s->pf_gate);
-        linear(s->pf_xn, W(l, MLB_W_UP), n, D, F, nullptr, s->pf_up);
+        linear(s->pf_xn, W(l, MLB_W_UP), n, D, F, nullptr, s->pf_up, true);
         Launch("RowsSwigluKernel", RowsSwigluKernel, dim3(RowsGrid(size_t(n) * F, 256, c.sm_count)), dim3(256), 0,
                st, true, const_cast<const float*>(s->pf_gate), const_cast<const float*>(s->pf_up), size_t(n) * F,
                s->pf_sw);
