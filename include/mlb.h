@@ -86,9 +86,11 @@ int mlb_synchronize(int device);
  * replaces include/cuda_quant.h:13-38 (CudaQ80/Q40/Q41 Linear, ...DeviceWeight,
  * ...DeviceInput), reference kernels src/cuda_quant.cu:40-135.
  * block_count must equal out * ceil(in/32) (the reference's check,
- * src/cuda_quant.cu:175-181).  bias may be NULL.  rows <= 8 runs the
- * bandwidth-bound bulk-copy GEMV; larger batches use the tensor-core path
- * when available. */
+ * src/cuda_quant.cu:175-181).  bias may be NULL.  rows <= 8 runs a
+ * bandwidth-bound GEMV over the blocks (the integer tensor-core one on
+ * matrices with many 16-row tiles, such as an lm_head; launches of it are
+ * ordered on the library's stream, which its tile scheduler relies on);
+ * larger batches use the tcgen05 tensor-core linear. */
 int mlb_q80_linear(int device, const float* x, const void* w, size_t block_count, int rows,
                    int in_features, int out_features, const float* bias, float* y);
 int mlb_q40_linear(int device, const float* x, const void* w, size_t block_count, int rows,
