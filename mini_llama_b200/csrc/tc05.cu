@@ -922,7 +922,9 @@ void LaunchTcT(DeviceContext& c, const float* x, const uint8_t* w, int M, int K,
     else LaunchTcKernel<QT, 1, false>(c, grid, a, wmap);
     if (p.splits > 1) {
         const size_t mn = size_t(M) * N;
-        const int g = static_cast<int>(std::min<size_t>((mn + 255) / 256, size_t(8) * c.sm_count));
+        // four columns per thread when N % 4 == 0 (TcReduce's vector path)
+        const size_t items = (N & 3) == 0 ? mn / 4 : mn;
+        const int g = static_cast<int>(std::max<size_t>(1, std::min<size_t>((items + 255) / 256, size_t(8) * c.sm_count)));
         Launch("TcReduce", TcReduce, dim3(g), dim3(256), 0, c.stream, true, static_cast<const float*>(part), p.splits,
                M, N, bias, y);
     }
