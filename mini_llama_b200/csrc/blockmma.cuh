@@ -27,14 +27,15 @@
 // X = rint(x * 2^(22-E)) = D2*2^16 + D1*2^8 + D0, and B column 3m + p holds
 // plane p, so ceil(3M/8) MMAs per block cover M rows of x.  The int32 sums
 // are exact; the accumulator starts at the bit pattern of 1.5*2^23, so the
-// result read as a float is 1.5*2^23 + S and one subtraction converts it.
-// Each column accumulates S * (plane weight * 2^(E-22) * d_r) over the
-// blocks; the three columns of an x row are added at the end of the tile.
-// Per (row r, x row m) a block adds
-//   Q8_0: d_r * 2^(E-22) * (65536 S2 + 256 S1 + S0)
-//   Q4_0: the same with unsigned nibbles n as A and the accumulator started
-//         at 1.5*2^23 - 8 sum_k D_p[k], which applies the 8 of (n - 8)
-//   Q4_1: d_r * (nibble sums as Q4_0 without the 8) + min_r * sum_k x_b[k].
+// result read as a float is 1.5*2^23 + S.  Each column accumulates
+// S * w * d_r over the blocks, w = plane weight * 2^(E-22): one FMA of the
+// raw result with w and -(1.5*2^23 + c) w gives (S - c) w exactly, a second
+// adds it times d_r; the three columns of an x row are added at the end of
+// the tile.  Per (row r, x row m) a block adds
+//   Q8_0: d_r * 2^(E-22) * (65536 S2 + 256 S1 + S0)           (c = 0)
+//   Q4_0: the same with unsigned nibbles n as A and c = 8 sum_k D_p[k],
+//         which applies the 8 of (n - 8)
+//   Q4_1: d_r * (nibble sums, c = 0) + min_r * sum_k x_b[k].
 // The only roundings are the rint of x (2^-23 of the block maximum) and the
 // fp32 combine, as in an fp32 dot product.
 //
