@@ -139,7 +139,10 @@ def test_linear_microbench_shapes(mlb, gpu, oracle, qtype, n, k, m):
 # 1024 (16 whole rows per copy, row pitch 0 mod 8 words), 576 (odd pitch in
 # words), 896 (pitch 2 mod 4 words: interleaved rows), 800 (odd block count:
 # Q4_1 here, the other GEMV for Q8_0 / Q4_0); every N ends on a partial tile.
-BLOCK_MMA_SHAPES = [(4099, 4864), (9475, 1024), (9475, 576), (9475, 896), (9475, 800)]
+# whole rows and split rows; last 32-row tiles of 3 rows (one half past the end)
+# and of 20 rows (the second half partly past the end)
+BLOCK_MMA_SHAPES = [(4099, 4864), (3572, 4864), (9475, 1024), (9475, 576), (9475, 896), (9492, 896),
+                    (9475, 800)]
 
 
 @pytest.mark.parametrize("qtype", [Q80, Q40, Q41])
@@ -149,7 +152,7 @@ def test_linear_block_mma_layouts(mlb, gpu, oracle, qtype, n, k):
     blocks = oracle.quantize(qtype, w)
     wdq = oracle.dequantize(qtype, blocks, n, k)
     bias = oracle.normal(n, 2, 3001, 0.1)
-    for m in (1, 3, 8):
+    for m in (1, 2, 3, 8):
         x = oracle.normal(m * k, 2, STREAM_X + 3000 + k + m, 1.0).reshape(m, k)
         expect = oracle.linear(qtype, x, blocks, n)
         assert_linear_close(linear_gpu(mlb, gpu, qtype, x, blocks, n), expect, linear_terms(x, wdq),
