@@ -5,7 +5,7 @@
 // Work: a row tile is 16 consecutive weight rows; a unit is one row tile over
 // kc consecutive blocks (kc = all blocks of the row when 16 rows fit a slot,
 // else a multiple of 8, so every piece of a row starts 16-byte aligned).  A
-// group of 2 or 4 warps owns whole row tiles (all their units in turn) and its
+// group of warps (a pair) owns whole row tiles (all their units in turn) and its
 // own ring of shared-memory slots; the leader moves a whole-row unit with one
 // bulk copy (16 GGUF rows are contiguous), a split unit with one bulk copy per
 // row (lanes 0..15), completing on the slot's mbarrier; weights are read once,
@@ -48,6 +48,11 @@
 namespace mlb {
 
 constexpr int kBmMaxWarps = 16;
+// Warps per group.  A compile-time constant: with the size read from the
+// parameters (divisions and loops at run time per unit) a call took 1.6 us
+// longer at one row of x on the [151936, 896] shape.  Groups of four
+// measured slower at every row count.
+constexpr int kBmGroupWarps = 2;
 constexpr uint32_t kBmMagic = 0x4B400000u;  // 1.5 * 2^23
 constexpr float kBmMagicF = 12582912.0f;
 
@@ -69,7 +74,7 @@ struct BmParams {
     int units_k;    // units per row tile (1: whole rows)
     int tiles;      // row tiles
     int slots;      // ring slots per warp group
-    int gsize;      // warps per group (2 or 4): they split each unit's blocks
+    int gsize;      // warps per group (kBmGroupWarps): they split each unit's blocks
     int stage_bytes;
     int pitch;      // bytes from one row of a unit to the next in shared memory
     int rowmap;     // 1: MMA rows g, g + 8 are tile rows 2g, 2g + 1; 0: g, g + 8
@@ -392,7 +397,7 @@ __global__ void __launch_bounds__(kBmMaxWarps * 32, 1) BlockMmaGemvKernel(const 
     constexpr int kCols = 8 * NJ;
     constexpr int kBB = BmTraits<QT>::kBytes;
     extern __shared__ __align__(128) uint8_t smem[];
-    const int gs = p.gsize;
+    constexpr int gs = kBmGroupWarps;
     const int nw = blockDim.x >> 5, ngroups = nw / gs;  // warp groups
     const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31, g = lane >> 2, t = lane & 3;
     const int grp = warp / gs, member = warp - grp * gs;

@@ -51,7 +51,11 @@ GemvPlan PlanGemv(GemvParams& p, int qtype, int M, bool dual, int sm_count, int 
     if (p.part_ml) p.aux_floats = p.n_heads * p.chunks * (p.head_dim + 2);
     plan.smem = GemvSmem::Bytes(M, p.nb, p.stage_bytes, p.aux_floats);
     if (plan.smem + 4096 > static_cast<size_t>(max_smem)) return plan;
-    plan.grid = std::max(1, std::min(total, sm_count * ctas_per_sm));
+    // no more CTAs than fit on the SMs at once (an SM's shared memory is the
+    // per-block maximum plus the 1 KB the runtime reserves per block): a
+    // second wave would stage x again and start its ring late
+    const int resident = std::max(1, static_cast<int>((static_cast<size_t>(max_smem) + 1024) / (plan.smem + 1024)));
+    plan.grid = std::max(1, std::min(total, sm_count * std::min(ctas_per_sm, resident)));
     plan.ok = true;
     return plan;
 }
@@ -84,14 +88,14 @@ BmPlan PlanBlockMma(BmParams& p, int qtype, int M, int sm_count, int max_smem) {
         return plan;
     }
     // Too few row tiles to stream: the other GEMV (K split across warps)
-    // finishes sooner below about 4 whole-row tiles per SM, or 1.5 tiles per
-    // SM when rows are split into pieces (each pair would run a tile's
-    // pieces one after another).
-    if (p.units_k == 1 ? p.tiles < 4 * sm_count : 2 * p.tiles < 3 * sm_count) return plan;
+    // finishes sooner below about 4 row tiles per SM (measured on whole rows
+    // and on rows split into pieces, where a pair runs a tile's pieces one
+    // after another).
+    if (p.tiles < 4 * sm_count) return plan;
     p.rowmap = ((p.pitch / 4) % 4 == 2) ? 1 : 0;
     // Warp pairs with a two-slot ring each (groups of 4 warps with 3 or 4
     // slots, splitting each tile 4 ways, measured slower at every row count)
-    p.gsize = 2;
+    p.gsize = kBmGroupWarps;
     p.slots = 2;
     const bool sums = qtype == MLB_Q4_1;
     const size_t budget = static_cast<size_t>(max_smem) - 1024;
@@ -253,12 +257,21 @@ void LinearRows(DeviceContext& c, int qtype, const float* x, const uint8_t* wb, 
         int M = std::min(rows - m0, kGemvMaxM);
         {
             // tensor-core GEMV over the blocks, when the shape suits it
-            BmParams bp = {};
-            bp.w = wb;
-            bp.K = in_features;
-            bp.N = out_features;
-            const BmPlan bplan = PlanBlockMma(bp, qtype, M, c.sm_count, c.max_smem_optin);
+            // (x's tables grow with the rows of x: when they leave too
+            // little room, fewer rows per launch)
+            BmParams bp;
+            BmPlan bplan;
+            int mb = M;
+            for (;; mb = (mb + 1) / 2) {
+                bp = BmParams{};
+                bp.w = wb;
+                bp.K = in_features;
+                bp.N = out_features;
+                bplan = PlanBlockMma(bp, qtype, mb, c.sm_count, c.max_smem_optin);
+                if (bplan.ok || mb == 1) break;
+            }
             if (bplan.ok) {
+                M = mb;
                 bp.x = x + static_cast<size_t>(m0) * in_features;
                 bp.y = y + static_cast<size_t>(m0) * out_features;
                 bp.bias = bias;

@@ -88,6 +88,25 @@ def time_case(lib, dev, torch, stream, qtype, n, k, m, reps=10):
     return secs, algo
 
 
+def path_of(qtype: int, n: int, k: int, m: int, sm_count: int) -> str:
+    """The kernel the library's planner picks (csrc/linear.cu LinearRows and
+    PlanBlockMma), restated for labelling: tcgen05 from 9 rows of x; below,
+    the integer-MMA GEMV ("block-mma") on shapes with at least 4 row tiles of
+    16 rows per SM, an even block count (Q8_0 / Q4_0) and whole rows within
+    20 KB per 16 rows or a 16-byte row pitch, else the SIMT GEMV ("gemv").
+    The shared-memory check of x's tables (long K at many rows, which makes
+    the library run fewer rows per launch) is not restated."""
+    if m >= 9:
+        return "tcgen05"
+    nb = (k + 31) // 32
+    rowbytes = nb * BLOCK_BYTES[qtype]
+    if (n + 15) // 16 < 4 * sm_count or (qtype != capi.Q4_1 and nb % 2):
+        return "gemv"
+    if 16 * rowbytes > 20 * 1024 and rowbytes % 16:
+        return "gemv"
+    return "block-mma"
+
+
 def main(argv=None) -> int:
     ap = argparse.ArgumentParser()
     ap.add_argument("--qtypes", default="q8_0,q4_0,q4_1")
@@ -101,6 +120,7 @@ def main(argv=None) -> int:
     torch.cuda.set_device(dev)
     stream = torch.cuda.ExternalStream(lib.stream(dev), device=torch.device("cuda", dev))
     pk = peaks()
+    sm_count = torch.cuda.get_device_properties(dev).multi_processor_count
     shapes = SHAPES if args.shapes == "all" else [tuple(int(v) for v in s.split("x")) for s in args.shapes.split(",")]
     for qn in args.qtypes.split(","):
         for n, k in shapes:
@@ -112,7 +132,7 @@ def main(argv=None) -> int:
                                   "gbs": round(gbs, 1), "hbm_frac": round(gbs / pk["hbm_gbs"], 3),
                                   "tflops": round(tflops, 2),
                                   "bf16_frac": round(tflops / pk["bf16_tflops"], 4),
-                                  "path": "tcgen05" if m >= 9 else "gemv", "peaks": pk["source"]}),
+                                  "path": path_of(QTYPES[qn], n, k, m, sm_count), "peaks": pk["source"]}),
                       flush=True)
     return 0
 

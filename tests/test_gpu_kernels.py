@@ -132,17 +132,15 @@ def test_linear_microbench_shapes(mlb, gpu, oracle, qtype, n, k, m):
                         linear_terms(x, bench_dequant(oracle, qtype, n, k)), f"{QNAME[qtype]} [{n},{k}] M={m}")
 
 
-# Shapes with enough 16-row tiles per SM (1.5 for split rows, 4 for whole
-# rows) to take the tensor-core GEMV over the blocks for 1..8 rows where x's
-# tables fit, covering its unit and bank layouts: K = 4864 (rows split into
-# 8-block pieces copied row by row; 3 and 8 rows of x take the other GEMV),
-# 1024 (16 whole rows per copy, row pitch 0 mod 8 words), 576 (odd pitch in
-# words), 896 (pitch 2 mod 4 words: interleaved rows), 800 (odd block count:
-# Q4_1 here, the other GEMV for Q8_0 / Q4_0); every N ends on a partial tile.
-# whole rows and split rows; last 32-row tiles of 3 rows (one half past the end)
-# and of 20 rows (the second half partly past the end)
-BLOCK_MMA_SHAPES = [(4099, 4864), (3572, 4864), (9475, 1024), (9475, 576), (9475, 896), (9492, 896),
-                    (9475, 800)]
+# Shapes with enough 16-row tiles per SM (4) to take the tensor-core GEMV over
+# the blocks for 1..8 rows, covering its unit and bank layouts: K = 4864 (rows
+# split into 8-block pieces copied row by row; at 8 rows of x its digit tables
+# leave too little room, so the call runs two launches of 4 rows), 1024 (16
+# whole rows per copy, row pitch 0 mod 8 words), 576 (odd pitch in words), 896
+# (pitch 2 mod 4 words: interleaved rows), 800 (odd block count: Q4_1 here,
+# the other GEMV for Q8_0 / Q4_0); every N ends on a partial tile (3 or 4
+# rows).
+BLOCK_MMA_SHAPES = [(9475, 4864), (9475, 1024), (9475, 576), (9475, 896), (9492, 896), (9475, 800)]
 
 
 @pytest.mark.parametrize("qtype", [Q80, Q40, Q41])
@@ -150,7 +148,7 @@ BLOCK_MMA_SHAPES = [(4099, 4864), (3572, 4864), (9475, 1024), (9475, 576), (9475
 def test_linear_block_mma_layouts(mlb, gpu, oracle, qtype, n, k):
     w = oracle.normal(n * k, 2, STREAM_W + 3000 + k, 0.02).reshape(n, k)
     blocks = oracle.quantize(qtype, w)
-    wdq = oracle.dequantize(qtype, blocks, n, k)
+    wdq = np.abs(np.asarray(oracle.dequantize(qtype, blocks, n, k), np.float32))  # |w| for the terms
     bias = oracle.normal(n, 2, 3001, 0.1)
     for m in (1, 2, 3, 8):
         x = oracle.normal(m * k, 2, STREAM_X + 3000 + k + m, 1.0).reshape(m, k)
@@ -164,7 +162,7 @@ def test_linear_block_mma_layouts(mlb, gpu, oracle, qtype, n, k):
 def test_linear_block_mma_repeated_calls(mlb, gpu, oracle):
     """The GEMV's tile scheduler resets itself at the end of every launch:
     calls in a row, of different shapes, each give the full result."""
-    cases = [(151936 // 8, 896, 1), (4099, 4864, 1), (9475, 896, 5)]
+    cases = [(151936 // 8, 896, 1), (9475, 4864, 8), (9475, 896, 5)]
     for rep in range(2):
         for (n, k, m) in cases:
             blocks = bench_blocks(oracle, Q80, n, k)
