@@ -90,7 +90,9 @@ int mlb_synchronize(int device);
  * bandwidth-bound GEMV over the blocks (the integer tensor-core one on
  * matrices with many 16-row tiles, such as an lm_head; launches of it are
  * ordered on the library's stream, which its tile scheduler relies on);
- * larger batches use the tcgen05 tensor-core linear. */
+ * 9..64 rows an integer-MMA linear (x's exact digit planes against the raw
+ * quants) where it is the faster one, other batches the tcgen05 tensor-core
+ * linear. */
 int mlb_q80_linear(int device, const float* x, const void* w, size_t block_count, int rows,
                    int in_features, int out_features, const float* bias, float* y);
 int mlb_q40_linear(int device, const float* x, const void* w, size_t block_count, int rows,
@@ -322,7 +324,7 @@ int mlb_session_test_withhold_signal(mlb_session* session, int counter);
 int mlb_session_kv_cache(mlb_session* session, float** key_cache, float** value_cache);
 /* Prompts of at least min_tokens tokens (default 16; 0: never) go through
  * mlb_session_generate in one pass -- every layer on all prompt tokens at
- * once, each linear one call on n_prompt rows (tcgen05 tensor cores from 9),
+ * once, each linear one call on n_prompt rows (tensor cores from 9 rows),
  * RoPE and the KV write for all positions, then causal attention as a batch
  * of queries over the cache -- instead of one decode step per token.  The
  * per-position computation is the same; the reference processes prompts one
@@ -333,7 +335,7 @@ int mlb_session_prefill_min(mlb_session* session, int min_tokens);
  * A batch of independent sequences decoded in lockstep through one model:
  * every step feeds one token per sequence (prompt tokens first, then the
  * greedy choice), so each linear runs on `batch` rows (the GEMV up to 8 rows,
- * the tcgen05 tensor cores from 9) and attention runs batched.  No reference
+ * the tensor cores from 9) and attention runs batched.  No reference
  * counterpart: the reference decodes one sequence at a time (ForwardBatch,
  * src/forward.cpp:668-684, loops ForwardToken); per sequence the computation
  * is that of mlb_session_generate, so the greedy tokens match it.

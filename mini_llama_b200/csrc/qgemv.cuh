@@ -553,6 +553,19 @@ void LaunchTcLinear(DeviceContext& c, int qtype, const float* x, const uint8_t* 
                     const float* bias, float* y, int* status, void* workspace = nullptr, bool reuse_x = false);
 size_t TcWorkspaceBytes(int M, int K, int N, int sm_count);
 
+// LaunchTcLinear first tries the integer-MMA linear (wide.cu: x's digit
+// tables from one pre-pass, GGUF blocks straight from a bulk-copy ring,
+// split-K sums in a deterministic pass) where it measured faster
+// (WidePreferred: up to 32 rows, or up to kWideMaxRows rows on weights of at
+// most 8 M elements); LaunchWideLinear returns false when the shape does not
+// suit it (odd block count of Q8_0 / Q4_0, misaligned weights).  Its
+// workspace (tables, partial sums) is part of TcWorkspaceBytes.
+constexpr int kWideMaxRows = 64;
+bool WidePreferred(int M, int K, int N);
+bool LaunchWideLinear(DeviceContext& c, int qtype, const float* x, const uint8_t* w, int M, int K, int N,
+                      const float* bias, float* y, int* status, void* workspace, bool reuse_x);
+size_t WideWorkspaceBytes(int M, int K, int N, int sm_count, int max_smem);
+
 // Quantized linear over GGUF blocks for any row count (the GEMV up to
 // kGemvMaxM rows at a time below kTcMinRows, the tensor cores above), on the
 // context's stream; tc_workspace as for LaunchTcLinear.

@@ -932,12 +932,18 @@ void LaunchTcT(DeviceContext& c, const float* x, const uint8_t* w, int M, int K,
 
 }  // namespace
 
-size_t TcWorkspaceBytes(int M, int K, int N, int sm_count) { return LayoutTc(M, K, N, sm_count).total; }
+size_t TcWorkspaceBytes(int M, int K, int N, int sm_count) {
+    size_t total = LayoutTc(M, K, N, sm_count).total;
+    if (WidePreferred(M, K, N)) total = std::max(total, WideWorkspaceBytes(M, K, N, sm_count, 227 * 1024));
+    return total;
+}
 
 void LaunchTcLinear(DeviceContext& c, int qtype, const float* x, const uint8_t* w, int M, int K, int N,
                     const float* bias, float* y, int* status, void* workspace, bool reuse_x) {
     static_assert(sizeof(TcShared) <= kTcHeader, "shared header");
     Require((reinterpret_cast<uintptr_t>(w) & 1) == 0, "mlb_quant_linear", "weight blocks must be 2-byte aligned");
+    if (WidePreferred(M, K, N) && LaunchWideLinear(c, qtype, x, w, M, K, N, bias, y, status, workspace, reuse_x))
+        return;
     switch (qtype) {
         case MLB_Q8_0: LaunchTcT<MLB_Q8_0>(c, x, w, M, K, N, bias, y, status, workspace, reuse_x); break;
         case MLB_Q4_0: LaunchTcT<MLB_Q4_0>(c, x, w, M, K, N, bias, y, status, workspace, reuse_x); break;

@@ -5,8 +5,9 @@
 Weights W ~ N(0, 0.02) (seeded generator on the device) quantized on the
 device to each block type; x ~ N(0, 1); shapes [N, K] = [896, 896],
 [4864, 896], [896, 4864], [151936, 896]; M rows of x.  Each case is timed
-through the public entry point (mlb_quant_linear: M <= 8 runs the GEMV, M >= 9
-the tcgen05 kernel, including its x pre-pass) with CUDA events on the
+through the public entry point (mlb_quant_linear: M <= 8 runs a GEMV, 9..64
+rows the integer-MMA linear or the tcgen05 kernel, more the tcgen05 kernel,
+including their x pre-passes) with CUDA events on the
 library stream, after warm-up, with the L2 flushed before every launch (a
 256 MB write, then a read of the same buffer, which leaves clean lines) and
 all reps queued before the first is waited for (device time, not host launch
@@ -90,15 +91,19 @@ def time_case(lib, dev, torch, stream, qtype, n, k, m, reps=10):
 
 def path_of(qtype: int, n: int, k: int, m: int, sm_count: int) -> str:
     """The kernel the library's planner picks (csrc/linear.cu LinearRows and
-    PlanBlockMma), restated for labelling: tcgen05 from 9 rows of x; below,
+    PlanBlockMma, csrc/wide.cu WidePreferred), restated for labelling: from 9
+    rows of x the integer-MMA linear ("int-mma") up to 32 rows, or up to 64 on
+    weights of at most 8 M elements (even block count for Q8_0 / Q4_0), else
+    tcgen05; below,
     the integer-MMA GEMV ("block-mma") on shapes with at least 4 row tiles of
     16 rows per SM, an even block count (Q8_0 / Q4_0) and whole rows within
     20 KB per 16 rows or a 16-byte row pitch, else the SIMT GEMV ("gemv").
     The shared-memory check of x's tables (long K at many rows, which makes
     the library run fewer rows per launch) is not restated."""
-    if m >= 9:
-        return "tcgen05"
     nb = (k + 31) // 32
+    if m >= 9:
+        wide = m <= 64 and (m <= 32 or n * k <= (8 << 20)) and (qtype == capi.Q4_1 or nb % 2 == 0)
+        return "int-mma" if wide else "tcgen05"
     rowbytes = nb * BLOCK_BYTES[qtype]
     if (n + 15) // 16 < 4 * sm_count or (qtype != capi.Q4_1 and nb % 2):
         return "gemv"
