@@ -56,6 +56,28 @@ def test_prefill_linear_ragged_with_bias(mlb, gpu, oracle, qtype, m, k, n):
                         linear_terms(x, oracle.dequantize(qtype, blocks, n, k), bias), f"{QNAME[qtype]} M={m} K={k} N={n}")
 
 
+# Shapes for the integer-MMA linear of 9..64 rows (csrc/wide.cu): x rows that
+# fill 8-row groups partly (17, 24, 40), block counts not a multiple of a
+# stage's four (Q4_1 only with an odd count: Q8_0 / Q4_0 then take the
+# tcgen05 kernel), output rows not a multiple of a CTA's 128, weight rows
+# viewed 1, 2 or 4 at a time by the tensor map, and N % 4 != 0 with 4 rows per
+# view (the per-row bulk-copy fallback), with bias, and the same call twice
+# (x's tables rebuilt, the split sums rewritten).
+@pytest.mark.parametrize("qtype", [Q80, Q40, Q41])
+@pytest.mark.parametrize("m,k,n", [(24, 1024, 262), (40, 896, 262), (17, 800, 262), (64, 96, 1000),
+                                   (32, 4864, 384)])
+def test_prefill_linear_int_mma_layouts(mlb, gpu, oracle, qtype, m, k, n):
+    w = oracle.normal(n * k, 2, STREAM_W + 5000 + n + k, 0.02).reshape(n, k)
+    blocks = oracle.quantize(qtype, w)
+    x = oracle.normal(m * k, 2, STREAM_X + 5000 + m + k, 1.0).reshape(m, k)
+    bias = oracle.normal(n, 2, 5999, 0.1)
+    expect = oracle.linear(qtype, x, blocks, n) + bias[None, :]
+    terms = linear_terms(x, oracle.dequantize(qtype, blocks, n, k), bias)
+    for rep in range(2):
+        assert_linear_close(linear_gpu(mlb, gpu, qtype, x, blocks, n, bias), expect, terms,
+                            f"{QNAME[qtype]} M={m} K={k} N={n} call {rep}")
+
+
 def test_prefill_linear_row_scales(mlb, gpu, oracle):
     """Rows of very different magnitude (1e-6 .. 1e4) keep their relative
     accuracy: each x row and W row has its own power-of-two scale."""
