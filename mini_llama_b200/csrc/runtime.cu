@@ -170,11 +170,17 @@ int mlb_memcpy_h2d(int device, void* dst, const void* src, size_t bytes) {
         if (bytes == 0) return;
         Require(dst && src, "mlb_memcpy_h2d", "cuda memcpy dst or src is nullptr");
         DeviceContext& c = Ctx(device);
+        // Pageable sources are staged by the driver before the copy call
+        // returns, so the caller may reuse them at once; pinned (or
+        // registered) sources are read asynchronously, so those copies are
+        // waited for.
+        cudaPointerAttributes attr{};
+        const cudaError_t ar = cudaPointerGetAttributes(&attr, src);
+        if (ar != cudaSuccess) cudaGetLastError();  // not a pointer CUDA knows: treat it as pinned, and wait
+        const bool pageable = ar == cudaSuccess && attr.type == cudaMemoryTypeUnregistered;
         CheckCuda(cudaMemcpyAsync(dst, src, bytes, cudaMemcpyHostToDevice, c.stream),
                   "cudaMemcpyAsync(H2D)");
-        // Pageable sources are staged by the driver before the call returns;
-        // pinned sources are read asynchronously, so wait for the copy.
-        CheckCuda(cudaStreamSynchronize(c.stream), "cudaStreamSynchronize(H2D)");
+        if (!pageable) CheckCuda(cudaStreamSynchronize(c.stream), "cudaStreamSynchronize(H2D)");
     });
 }
 
