@@ -641,6 +641,15 @@ void Prefill(mlb_session* s, DeviceContext& c, int start, int n) {
                       bool same_x = false) {
         LinearRows(c, qt, x, w, rows, K, N, bias, y, nullptr, same_x);
     };
+    // linears that read the same x (q / k / v, gate / up): one launch of the
+    // integer-MMA linear for all of them where that path takes each one, else
+    // one call each
+    auto linears = [&](const float* x, int rows, int K, const WideSeg* segs, int nseg) {
+        bool one = rows >= kTcMinRows && rows <= kWideMaxRows;
+        for (int i = 0; i < nseg && one; ++i) one = WidePreferred(rows, K, segs[i].N);
+        if (one && LaunchWideLinearSegs(c, qt, x, rows, K, segs, nseg, c.status, nullptr, false)) return;
+        for (int i = 0; i < nseg; ++i) linear(x, segs[i].w, rows, K, segs[i].N, segs[i].bias, segs[i].y, i > 0);
+    };
     auto rms = [&](const float* x, const float* w, float* y, int rows) {
         Launch("RowsRmsNormKernel", RowsRmsNormKernel, dim3(rows), dim3(256), 0, st, true, x, w, y, D,
                cf.rms_norm_eps);
@@ -656,9 +665,12 @@ void Prefill(mlb_session* s, DeviceContext& c, int start, int n) {
            const_cast<const int*>(s->hist + start), s->pf_x, status);
     for (int l = 0; l < cf.n_layers; ++l) {
         rms(s->pf_x, Fv(l, MLB_W_ATTN_NORM), s->pf_xn, n);
-        linear(s->pf_xn, W(l, MLB_W_WQ), n, D, qd, cf.qkv_bias ? Fv(l, MLB_W_BQ) : nullptr, s->pf_q);
-        linear(s->pf_xn, W(l, MLB_W_WK), n, D, kd, cf.qkv_bias ? Fv(l, MLB_W_BK) : nullptr, s->pf_k, true);
-        linear(s->pf_xn, W(l, MLB_W_WV), n, D, kd, cf.qkv_bias ? Fv(l, MLB_W_BV) : nullptr, s->pf_v, true);
+        {
+            const WideSeg qkv[3] = {{W(l, MLB_W_WQ), cf.qkv_bias ? Fv(l, MLB_W_BQ) : nullptr, s->pf_q, qd},
+                                    {W(l, MLB_W_WK), cf.qkv_bias ? Fv(l, MLB_W_BK) : nullptr, s->pf_k, kd},
+                                    {W(l, MLB_W_WV), cf.qkv_bias ? Fv(l, MLB_W_BV) : nullptr, s->pf_v, kd}};
+            linears(s->pf_xn, n, D, qkv, 3);
+        }
         Launch("RowsRopeKvKernel", RowsRopeKvKernel, dim3(n), dim3(256), 0, st, true, s->pf_q,
                const_cast<const float*>(s->pf_k), const_cast<const float*>(s->pf_v), cf.n_heads, cf.n_kv_heads, hd,
                start, const_cast<const float*>(m->rope_cos), const_cast<const float*>(m->rope_sin),
@@ -692,8 +704,10 @@ void Prefill(mlb_session* s, DeviceContext& c, int start, int n) {
         linear(s->pf_attn, W(l, MLB_W_WO), n, qd, D, nullptr, s->pf_o);
         add(s->pf_x, s->pf_o, s->pf_xmid, size_t(n) * D);
         rms(s->pf_xmid, Fv(l, MLB_W_FFN_NORM), s->pf_xn, n);
-        linear(s->pf_xn, W(l, MLB_W_GATE), n, D, F, nullptr, s->pf_gate);
-        linear(s->pf_xn, W(l, MLB_W_UP), n, D, F, nullptr, s->pf_up, true);
+        {
+            const WideSeg gu[2] = {{W(l, MLB_W_GATE), nullptr, s->pf_gate, F}, {W(l, MLB_W_UP), nullptr, s->pf_up, F}};
+            linears(s->pf_xn, n, D, gu, 2);
+        }
         Launch("RowsSwigluKernel", RowsSwigluKernel, dim3(RowsGrid(size_t(n) * F, 256, c.sm_count)), dim3(256), 0,
                st, true, const_cast<const float*>(s->pf_gate), const_cast<const float*>(s->pf_up), size_t(n) * F,
                s->pf_sw);

@@ -565,6 +565,18 @@ bool WidePreferred(int M, int K, int N);
 bool LaunchWideLinear(DeviceContext& c, int qtype, const float* x, const uint8_t* w, int M, int K, int N,
                       const float* bias, float* y, int* status, void* workspace, bool reuse_x);
 size_t WideWorkspaceBytes(int M, int K, int N, int sm_count, int max_smem);
+// Several weight matrices (up to 3) that read the same x, same K and block
+// type, in one launch of the integer-MMA linear (the x pre-pass once, the
+// matrices' row groups side by side in the grid); false when the shape does
+// not suit it.  Workspace: null for the context's grow-only workspace.
+struct WideSeg {
+    const uint8_t* w;
+    const float* bias;
+    float* y;
+    int N;
+};
+bool LaunchWideLinearSegs(DeviceContext& c, int qtype, const float* x, int M, int K, const WideSeg* segs, int nseg,
+                          int* status, void* workspace, bool reuse_x);
 
 // Quantized linear over GGUF blocks for any row count (the GEMV up to
 // kGemvMaxM rows at a time below kTcMinRows, the tensor cores above), on the

@@ -70,19 +70,26 @@ struct WTraits<MLB_Q4_1> {
 __host__ __device__ constexpr int WTabBlock(int MQ) { return 3 * MQ * 512 + 3 * MQ * 128 + MQ * 64; }
 __host__ __device__ constexpr int WTabSums(int MQ) { return 3 * MQ * 640; }
 
+// One launch covers up to kWMaxSegs weight matrices that read the same x
+// (same K and block type): their row groups follow one another in the grid.
+constexpr int kWMaxSegs = 3;
+
 struct WideParams {
-    const uint8_t* w;    // GGUF blocks [N, nb], 16-byte aligned
+    const uint8_t* w[kWMaxSegs];  // GGUF blocks [N_s, nb], 16-byte aligned
+    const float* bias[kWMaxSegs];  // [N_s] or null (applied here when splits == 1)
+    float* y[kWMaxSegs];           // [M, N_s]
+    float* part[kWMaxSegs];        // partial sums [splits][M][N_s] (splits > 1)
+    int N[kWMaxSegs];
+    int tma_rows[kWMaxSegs];       // P > 0: rows arrive as P tensor-map boxes per stage; 0: one bulk copy per row
+    int rg_end[kWMaxSegs];         // row groups of segments 0..s together
+    int nseg;
     const uint8_t* tab;  // x tables [nb][WTabBlock(MQ)]
-    const float* bias;   // [N] or null (applied here when splits == 1)
-    float* y;            // [M, N]
-    float* part;         // partial sums [splits][M][N] (splits > 1)
-    int M, N, nb, rowbytes;
+    int M, nb, rowbytes;
     int kper;            // blocks per split (a multiple of kWBlocks)
     int splits;
     int pitch;           // bytes per weight row in a stage
     int stage_bytes;     // kWRows * pitch + kWBlocks * WTabBlock(MQ)
     int stages;          // ring stages (2..kWMaxStages)
-    int tma_rows;        // P > 0: rows arrive as P tensor-map boxes per stage; 0: one bulk copy per row
     int* status;
 };
 
@@ -227,7 +234,9 @@ __global__ void __launch_bounds__(256) WideReduce(const float* part, int splits,
 // copies in flight.
 template <int QT, int MQ>
 __global__ void __launch_bounds__(kWThreads, 1) WideGemvKernel(const WideParams p,
-                                                                const __grid_constant__ CUtensorMap wmap) {
+                                                                const __grid_constant__ CUtensorMap wmap0,
+                                                                const __grid_constant__ CUtensorMap wmap1,
+                                                                const __grid_constant__ CUtensorMap wmap2) {
     constexpr int NF = 3 * MQ;
     constexpr int kBB = WTraits<QT>::kBytes;
     constexpr int kTab = WTabBlock(MQ);
@@ -238,7 +247,18 @@ __global__ void __launch_bounds__(kWThreads, 1) WideGemvKernel(const WideParams 
     volatile int* abort = reinterpret_cast<volatile int*>(empty + kWMaxStages);
     uint8_t* stages = smem + kWHeader;
     const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31, g = lane >> 2, t = lane & 3;
-    const int n0 = blockIdx.x * kWRows, sp = blockIdx.y;
+    // this CTA's weight matrix (fields picked with constant indices, so the
+    // parameters stay where they are)
+    int seg = 0;
+    if (p.nseg > 1 && static_cast<int>(blockIdx.x) >= p.rg_end[0]) seg = 1;
+    if (p.nseg > 2 && static_cast<int>(blockIdx.x) >= p.rg_end[1]) seg = 2;
+    auto pick = [&](auto a0, auto a1, auto a2) { return seg == 0 ? a0 : (seg == 1 ? a1 : a2); };
+    const uint8_t* const W = pick(p.w[0], p.w[1], p.w[2]);
+    const int N = pick(p.N[0], p.N[1], p.N[2]);
+    const int tma = pick(p.tma_rows[0], p.tma_rows[1], p.tma_rows[2]);
+    const CUtensorMap* const wmap = pick(&wmap0, &wmap1, &wmap2);
+    const int rg_first = seg == 0 ? 0 : pick(0, p.rg_end[0], p.rg_end[1]);
+    const int n0 = (static_cast<int>(blockIdx.x) - rg_first) * kWRows, sp = blockIdx.y;
     const int kb0 = sp * p.kper, kb1 = min(p.nb, kb0 + p.kper);
     const int nst = (kb1 - kb0 + kWBlocks - 1) / kWBlocks;
     const size_t rowbytes = static_cast<size_t>(p.rowbytes);
@@ -255,7 +275,7 @@ __global__ void __launch_bounds__(kWThreads, 1) WideGemvKernel(const WideParams 
 
     if (warp == kWWarps) {
         // ---------------------------------------------------------- producer
-        const uintptr_t wend = reinterpret_cast<uintptr_t>(p.w) + size_t(p.N) * rowbytes;
+        const uintptr_t wend = reinterpret_cast<uintptr_t>(W) + size_t(N) * rowbytes;
         auto fail = [&]() {
             if (lane == 0) {
                 *abort = 1;
@@ -267,16 +287,16 @@ __global__ void __launch_bounds__(kWThreads, 1) WideGemvKernel(const WideParams 
             const int slot = s % ns;
             const int b0 = kb0 + s * kWBlocks, nblk = min(kWBlocks, kb1 - b0);
             uint8_t* st = stages + size_t(slot) * p.stage_bytes;
-            if (p.tma_rows) {
+            if (tma) {
                 // P boxes of (pitch bytes x 128 / P rows): weight row P i + j
                 // lands in box j, row i (rows past N and bytes past a row read
                 // as zeros)
                 if (lane == 0) {
-                    const int P = p.tma_rows, rows = kWRows / P;
+                    const int P = tma, rows = kWRows / P;
                     MbarExpectTx(&full[slot], static_cast<uint32_t>(kWRows * p.pitch + nblk * kTab));
                     const long long k0 = static_cast<long long>(b0) * kBB;
                     for (int j = 0; j < P; ++j)
-                        WTmaLoad2D(st + size_t(j) * rows * p.pitch, &wmap,
+                        WTmaLoad2D(st + size_t(j) * rows * p.pitch, wmap,
                                    static_cast<int>((j * static_cast<long long>(rowbytes) + k0) & ~15LL), n0 / P,
                                    &full[slot]);
                 }
@@ -290,8 +310,8 @@ __global__ void __launch_bounds__(kWThreads, 1) WideGemvKernel(const WideParams 
             uint32_t len[4];
 #pragma unroll
             for (int i = 0; i < 4; ++i) {
-                const int n = min(n0 + lane + 32 * i, p.N - 1);
-                src[i] = reinterpret_cast<uintptr_t>(p.w) + size_t(n) * rowbytes + size_t(b0) * kBB;
+                const int n = min(n0 + lane + 32 * i, N - 1);
+                src[i] = reinterpret_cast<uintptr_t>(W) + size_t(n) * rowbytes + size_t(b0) * kBB;
                 const uintptr_t end = src[i] + size_t(nblk) * kBB;
                 s16[i] = src[i] & ~uintptr_t(15);
                 uintptr_t l = (end - s16[i] + 15) & ~uintptr_t(15);
@@ -354,15 +374,15 @@ __global__ void __launch_bounds__(kWThreads, 1) WideGemvKernel(const WideParams 
     // kRW rg + 8 j + 2 t, + 1), each with its row's byte offset mod 16 in the
     // weight buffer; with P boxes per stage, weight row r sits at stage row
     // (r % P) 128 / P + r / P
-    auto srow = [&](int r) { return p.tma_rows > 1 ? (r % p.tma_rows) * (kWRows / p.tma_rows) + r / p.tma_rows : r; };
+    auto srow = [&](int r) { return tma > 1 ? (r % tma) * (kWRows / tma) + r / tma : r; };
     int rq[kWJ], rd0[kWJ], rd1[kWJ];
     uint32_t mq[kWJ], md0[kWJ], md1[kWJ];
 #pragma unroll
     for (int j = 0; j < kWJ; ++j) {
         const int a = kRW * rg + 8 * j + g, b = kRW * rg + 8 * j + 2 * t;
-        mq[j] = static_cast<uint32_t>((size_t(min(n0 + a, p.N - 1)) * rowbytes) & 15);
-        md0[j] = static_cast<uint32_t>((size_t(min(n0 + b, p.N - 1)) * rowbytes) & 15);
-        md1[j] = static_cast<uint32_t>((size_t(min(n0 + b + 1, p.N - 1)) * rowbytes) & 15);
+        mq[j] = static_cast<uint32_t>((size_t(min(n0 + a, N - 1)) * rowbytes) & 15);
+        md0[j] = static_cast<uint32_t>((size_t(min(n0 + b, N - 1)) * rowbytes) & 15);
+        md1[j] = static_cast<uint32_t>((size_t(min(n0 + b + 1, N - 1)) * rowbytes) & 15);
         rq[j] = srow(a);
         rd0[j] = srow(b);
         rd1[j] = srow(b + 1);
@@ -527,16 +547,17 @@ __global__ void __launch_bounds__(kWThreads, 1) WideGemvKernel(const WideParams 
     if (kg == 1) return;
     GridDepWait();  // the outputs may still be read by earlier kernels until they finish
     const bool single = p.splits == 1;
-    float* out = single ? p.y : p.part + size_t(sp) * p.M * p.N;
+    const float* const bias = pick(p.bias[0], p.bias[1], p.bias[2]);
+    float* out = single ? pick(p.y[0], p.y[1], p.y[2]) : pick(p.part[0], p.part[1], p.part[2]) + size_t(sp) * p.M * N;
 #pragma unroll
     for (int q = 0; q < MQ; ++q)
 #pragma unroll
         for (int j = 0; j < kWJ; ++j) {
             const int n = n0 + kRW * rg + 8 * j + 2 * t;
             float b0v = 0.0f, b1v = 0.0f;
-            if (single && p.bias) {
-                if (n < p.N) b0v = p.bias[n];
-                if (n + 1 < p.N) b1v = p.bias[n + 1];
+            if (single && bias) {
+                if (n < N) b0v = bias[n];
+                if (n + 1 < N) b1v = bias[n + 1];
             }
 #pragma unroll
             for (int r = 0; r < 2; ++r) {
@@ -544,9 +565,9 @@ __global__ void __launch_bounds__(kWThreads, 1) WideGemvKernel(const WideParams 
                 if (m >= p.M) continue;
                 const float2 o = xch[((q * kWJ + j) * 2 + r) * 32 + lane];
                 const float2 v = make_float2(acc[q][j][r].x + o.x, acc[q][j][r].y + o.y);
-                float* yr = out + size_t(m) * p.N;
-                if (n < p.N) yr[n] = v.x + b0v;
-                if (n + 1 < p.N) yr[n + 1] = v.y + b1v;
+                float* yr = out + size_t(m) * N;
+                if (n < N) yr[n] = v.x + b0v;
+                if (n + 1 < N) yr[n + 1] = v.y + b1v;
             }
         }
 }
@@ -557,17 +578,17 @@ struct WidePlan {
     size_t smem = 0, tab_bytes = 0, part_off = 0, total = 0;
 };
 
-// Stage geometry and the block split: the split count minimises a cost in
-// SM cycles -- waves of CTAs x (blocks per split x the MMA time of a block,
-// 48 MQ MMAs at about 2.1 cycles each, plus a fixed cost per CTA) -- plus the
+// Stage geometry and the block split for `row_groups` CTAs' worth of weight
+// rows (n_total rows in all): the split count minimises a cost in SM cycles
+// -- waves of CTAs x (blocks per split x the MMA time of a block, 48 MQ MMAs
+// at about 2.1 cycles each, plus a fixed cost per CTA) -- plus the
 // partial-sum pass (its bytes at about 25 B per cycle per SM).
-WidePlan PlanWide(int qtype, int M, int K, int N, int sms, int max_smem, const void* w) {
+WidePlan PlanWide(int qtype, int M, int K, int row_groups, long long n_total, int sms, int max_smem) {
     WidePlan pl;
-    if (M < 1 || M > kWideMaxRows || K < 1 || N < 1) return pl;
+    if (M < 1 || M > kWideMaxRows || K < 1 || row_groups < 1) return pl;
     const int bb = BlockBytes(qtype);
     const int nb = (K + 31) / 32;
     if (qtype != MLB_Q4_1 && (nb & 1)) return pl;  // Q8_0 / Q4_0 blocks are read in pairs
-    if (reinterpret_cast<uintptr_t>(w) & 15) return pl;
     pl.MQ = (M + 15) / 16;
     // a row's range plus its misalignment, rounded to 16 bytes, at a pitch of
     // 4 mod 8 words: the eight rows one fragment load touches start in
@@ -580,17 +601,17 @@ WidePlan PlanWide(int qtype, int M, int K, int N, int sms, int max_smem, const v
                               static_cast<int>((static_cast<size_t>(max_smem) - 1024 - kWHeader) / pl.stage_bytes));
     if (pl.stages < 2) return pl;
     pl.smem = kWHeader + size_t(pl.stages) * pl.stage_bytes;
-    pl.row_groups = (N + kWRows - 1) / kWRows;
+    pl.row_groups = row_groups;
     const double blk = 48.0 * pl.MQ * 2.13, fixed = 5000.0;
     double best = 1e300;
     for (int s = 1; s <= 32; ++s) {
         const int kper = ((nb + s - 1) / s + kWBlocks - 1) / kWBlocks * kWBlocks;
         const int splits = (nb + kper - 1) / kper;
         if (splits != s) continue;
-        const long long ctas = static_cast<long long>(pl.row_groups) * splits;
+        const long long ctas = static_cast<long long>(row_groups) * splits;
         const long long waves = (ctas + sms - 1) / sms;
         double t = double(waves) * (kper * blk + fixed);
-        if (splits > 1) t += 2000.0 + double(M) * N * 4.0 * (splits + 1) / (25.0 * sms);
+        if (splits > 1) t += 2000.0 + double(M) * n_total * 4.0 * (splits + 1) / (25.0 * sms);
         if (t < best) {
             best = t;
             pl.kper = kper;
@@ -599,7 +620,7 @@ WidePlan PlanWide(int qtype, int M, int K, int N, int sms, int max_smem, const v
     }
     pl.tab_bytes = size_t(nb) * WTabBlock(pl.MQ);
     pl.part_off = (pl.tab_bytes + 255) / 256 * 256;
-    pl.total = pl.part_off + (pl.splits > 1 ? size_t(pl.splits) * M * N * 4 : 0);
+    pl.total = pl.part_off + (pl.splits > 1 ? size_t(pl.splits) * M * size_t(n_total) * 4 : 0);
     pl.ok = true;
     return pl;
 }
@@ -627,8 +648,8 @@ int WideWeightMap(const uint8_t* w, int N, size_t rowbytes, int pitch, CUtensorM
 }
 
 template <int QT, int MQ>
-void LaunchWideT(DeviceContext& c, const WidePlan& pl, const float* x, const uint8_t* w, int M, int K, int N,
-                 const float* bias, float* y, int* status, uint8_t* ws, bool reuse_x) {
+void LaunchWideT(DeviceContext& c, const WidePlan& pl, const float* x, int M, int K, const WideSeg* segs, int nseg,
+                 int* status, uint8_t* ws, bool reuse_x) {
     const int nb = (K + 31) / 32;
     const bool reuse = reuse_x && c.tc_x == x && c.tc_ws == ws && c.tc_m == M && c.tc_k == K && c.tc_mx == 0 &&
                        c.tc_mtiles == MQ;
@@ -641,11 +662,35 @@ void LaunchWideT(DeviceContext& c, const WidePlan& pl, const float* x, const uin
     c.tc_k = K;
     c.tc_mx = 0;  // marks this path's tables (the tcgen05 path's x images have tc_mx >= 16)
     c.tc_mtiles = MQ;
+    WideParams p{};
+    p.nseg = nseg;
+    p.tab = ws;
+    p.M = M;
+    p.nb = nb;
+    p.rowbytes = nb * BlockBytes(QT);
+    p.kper = pl.kper;
+    p.splits = pl.splits;
+    p.pitch = pl.pitch;
+    p.stage_bytes = pl.stage_bytes;
+    p.stages = pl.stages;
+    p.status = status;
+    CUtensorMap maps[kWMaxSegs];
     float* part = reinterpret_cast<float*>(ws + pl.part_off);
-    WideParams p{w, ws, bias, y, part, M, N, nb, nb * BlockBytes(QT), pl.kper, pl.splits,
-                 pl.pitch, pl.stage_bytes, pl.stages, 0, status};
-    CUtensorMap wmap;
-    p.tma_rows = WideWeightMap(w, N, size_t(p.rowbytes), pl.pitch, wmap);
+    int rg = 0;
+    for (int i = 0; i < kWMaxSegs; ++i) {
+        const int j = i < nseg ? i : nseg - 1;  // unused slots repeat the last segment
+        p.w[i] = segs[j].w;
+        p.bias[i] = segs[j].bias;
+        p.y[i] = segs[j].y;
+        p.N[i] = segs[j].N;
+        p.part[i] = part;
+        p.tma_rows[i] = WideWeightMap(segs[j].w, segs[j].N, size_t(p.rowbytes), pl.pitch, maps[i]);
+        if (i < nseg) {
+            rg += (segs[i].N + kWRows - 1) / kWRows;
+            part += size_t(pl.splits) * M * segs[i].N;
+        }
+        p.rg_end[i] = rg;
+    }
     static int configured[64] = {};
     if (c.device >= 64 || configured[c.device] < static_cast<int>(pl.smem)) {
         CheckCuda(cudaFuncSetAttribute(WideGemvKernel<QT, MQ>, cudaFuncAttributeMaxDynamicSharedMemorySize,
@@ -654,23 +699,25 @@ void LaunchWideT(DeviceContext& c, const WidePlan& pl, const float* x, const uin
         if (c.device < 64) configured[c.device] = static_cast<int>(pl.smem);
     }
     Launch("WideGemvKernel", WideGemvKernel<QT, MQ>, dim3(pl.row_groups, pl.splits), dim3(kWThreads), pl.smem,
-           c.stream, true, p, wmap);
+           c.stream, true, p, maps[0], maps[1], maps[2]);
     if (pl.splits > 1) {
-        const size_t mn = size_t(M) * N;
-        const int g = static_cast<int>(std::max<size_t>(1, std::min<size_t>((mn + 255) / 256, size_t(8) * c.sm_count)));
-        Launch("WideReduce", WideReduce, dim3(g), dim3(256), 0, c.stream, true, static_cast<const float*>(part),
-               pl.splits, M, N, bias, y);
+        for (int i = 0; i < nseg; ++i) {
+            const size_t mn = size_t(M) * segs[i].N;
+            const int g = static_cast<int>(std::max<size_t>(1, std::min<size_t>((mn + 255) / 256, size_t(8) * c.sm_count)));
+            Launch("WideReduce", WideReduce, dim3(g), dim3(256), 0, c.stream, true, static_cast<const float*>(p.part[i]),
+                   pl.splits, M, segs[i].N, segs[i].bias, segs[i].y);
+        }
     }
 }
 
 template <int QT>
-void LaunchWideQ(DeviceContext& c, const WidePlan& pl, const float* x, const uint8_t* w, int M, int K, int N,
-                 const float* bias, float* y, int* status, uint8_t* ws, bool reuse_x) {
+void LaunchWideQ(DeviceContext& c, const WidePlan& pl, const float* x, int M, int K, const WideSeg* segs, int nseg,
+                 int* status, uint8_t* ws, bool reuse_x) {
     switch (pl.MQ) {
-        case 1: return LaunchWideT<QT, 1>(c, pl, x, w, M, K, N, bias, y, status, ws, reuse_x);
-        case 2: return LaunchWideT<QT, 2>(c, pl, x, w, M, K, N, bias, y, status, ws, reuse_x);
-        case 3: return LaunchWideT<QT, 3>(c, pl, x, w, M, K, N, bias, y, status, ws, reuse_x);
-        default: return LaunchWideT<QT, 4>(c, pl, x, w, M, K, N, bias, y, status, ws, reuse_x);
+        case 1: return LaunchWideT<QT, 1>(c, pl, x, M, K, segs, nseg, status, ws, reuse_x);
+        case 2: return LaunchWideT<QT, 2>(c, pl, x, M, K, segs, nseg, status, ws, reuse_x);
+        case 3: return LaunchWideT<QT, 3>(c, pl, x, M, K, segs, nseg, status, ws, reuse_x);
+        default: return LaunchWideT<QT, 4>(c, pl, x, M, K, segs, nseg, status, ws, reuse_x);
     }
 }
 
@@ -683,24 +730,37 @@ bool WidePreferred(int M, int K, int N) {
 size_t WideWorkspaceBytes(int M, int K, int N, int sm_count, int max_smem) {
     size_t total = 0;
     for (int qt : {MLB_Q8_0, MLB_Q4_0, MLB_Q4_1}) {
-        // only the geometry matters here: any 16-byte aligned weight pointer
-        const WidePlan pl = PlanWide(qt, M, K, N, sm_count, max_smem, nullptr);
+        const WidePlan pl = PlanWide(qt, M, K, (N + kWRows - 1) / kWRows, N, sm_count, max_smem);
         if (pl.ok) total = std::max(total, pl.total);
     }
     return total;
 }
 
-bool LaunchWideLinear(DeviceContext& c, int qtype, const float* x, const uint8_t* w, int M, int K, int N,
-                      const float* bias, float* y, int* status, void* workspace, bool reuse_x) {
-    const WidePlan pl = PlanWide(qtype, M, K, N, c.sm_count, c.max_smem_optin, w);
+bool LaunchWideLinearSegs(DeviceContext& c, int qtype, const float* x, int M, int K, const WideSeg* segs, int nseg,
+                          int* status, void* workspace, bool reuse_x) {
+    if (nseg < 1 || nseg > kWMaxSegs) return false;
+    int row_groups = 0;
+    long long n_total = 0;
+    for (int i = 0; i < nseg; ++i) {
+        if (segs[i].N < 1 || (reinterpret_cast<uintptr_t>(segs[i].w) & 15)) return false;
+        row_groups += (segs[i].N + kWRows - 1) / kWRows;
+        n_total += segs[i].N;
+    }
+    const WidePlan pl = PlanWide(qtype, M, K, row_groups, n_total, c.sm_count, c.max_smem_optin);
     if (!pl.ok) return false;
     uint8_t* ws = static_cast<uint8_t*>(workspace ? workspace : Workspace(c, pl.total));
     switch (qtype) {
-        case MLB_Q8_0: LaunchWideQ<MLB_Q8_0>(c, pl, x, w, M, K, N, bias, y, status, ws, reuse_x); break;
-        case MLB_Q4_0: LaunchWideQ<MLB_Q4_0>(c, pl, x, w, M, K, N, bias, y, status, ws, reuse_x); break;
-        default: LaunchWideQ<MLB_Q4_1>(c, pl, x, w, M, K, N, bias, y, status, ws, reuse_x); break;
+        case MLB_Q8_0: LaunchWideQ<MLB_Q8_0>(c, pl, x, M, K, segs, nseg, status, ws, reuse_x); break;
+        case MLB_Q4_0: LaunchWideQ<MLB_Q4_0>(c, pl, x, M, K, segs, nseg, status, ws, reuse_x); break;
+        default: LaunchWideQ<MLB_Q4_1>(c, pl, x, M, K, segs, nseg, status, ws, reuse_x); break;
     }
     return true;
+}
+
+bool LaunchWideLinear(DeviceContext& c, int qtype, const float* x, const uint8_t* w, int M, int K, int N,
+                      const float* bias, float* y, int* status, void* workspace, bool reuse_x) {
+    const WideSeg seg{w, bias, y, N};
+    return LaunchWideLinearSegs(c, qtype, x, M, K, &seg, 1, status, workspace, reuse_x);
 }
 
 }  // namespace mlb
