@@ -26,9 +26,10 @@ def test_prefill_linear_microbench_shapes(mlb, gpu, oracle, qtype, n, k, m):
 
 
 @pytest.mark.parametrize("qtype", [Q80, Q40, Q41])
-@pytest.mark.parametrize("m", [64, 512])
+@pytest.mark.parametrize("m", [16, 32, 64, 512])
 def test_prefill_linear_lm_head(mlb, gpu, oracle, qtype, m):
-    """The lm_head shape on the tensor cores; at 512 rows every 16th row is
+    """The lm_head shape: 16 and 32 rows on the integer-MMA linear (1187 row
+    groups), 64 and more on the tcgen05 kernel; at 512 rows every 16th row is
     checked against the oracle (the full fp32 CPU product is 70 G
     multiply-adds)."""
     n, k = 151936, 896
